@@ -1,0 +1,353 @@
+"""Benchmark of the in-context sparse attention call (BASELINE metric:
+"sparse-attn ms/call at 65K joint tokens (40h x 128d bf16) 1/2/4/8 GPU").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload 480p|720p|config1]
+                    [--impl b200|reference]
+
+One step is one whole call over all 40 heads.  With N GPUs (torchrun, one
+process per GPU) the heads are split N ways (40/20/10/5 per GPU), every rank
+runs its shard with no collective on the data path, and the step time is the
+maximum over ranks: total work per call is fixed, so scaling is "strong".
+
+* value: ms per call with q/k/v resident in HBM, timed with CUDA events on
+  the launching stream around exactly K steps (barrier + synchronize on both
+  sides, max over ranks); the inputs (2 GB) are larger than L2.
+* e2e: the same call through the public Python API with q/k/v copied from
+  pinned host memory and the output copied back inside the timed region.
+* roofline: the attention kernel (stage 3, tensor-core bound), algorithmic
+  FLOPs per launch / its CUDA-event duration, against the measured
+  sustained bf16 peak.
+* cpu_baseline / --impl reference: the CPU restatement of the reference path
+  (the reference's PyTorch orchestration + restated kernels) on the host
+  cores, on a bounded sample of the same workload scaled to ms/call.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(REPO, "lightning-unified-video-editor-via-in-context-sparse-attention_b200")
+sys.path.insert(0, REPO)
+sys.path.insert(0, PKG_DIR)
+
+from in_context_sparse_attention import _capi, editing_sparse_attention, synthetic  # noqa: E402
+
+METRIC = "sparse-attn ms/call at 65K joint tokens (40h×128d bf16) 1/2/4/8 GPU; DiT step s"
+WORKLOADS = {"480p": synthetic.WAN480P, "720p": synthetic.WAN720P, "config1": synthetic.CONFIG1}
+KERNELS_PER_CALL_ALIGNED = 10  # pool, scores, rowstats, outc, colsum, 2x sort, extended-KV, top-k, attention
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops_sustained", 1373.7), d.get("bf16_tflops", 1626.6), d.get("hbm_gbs", 6546.9), "measured"
+    return 1400.0, 1590.0, 6650.0, "fallback"
+
+
+def attention_flops(p, n_sparse):
+    """Algorithmic FLOPs of the attention kernel per call (2 FLOP per MAC):
+    flat 4*Tq*Tkv*D, exact 4*Tq*(top_k*64)*D, interval 4*Tq*nkv*D."""
+    D, BH = p.D, p.B * p.H
+    flat = 4.0 * p.num_flat * 64 * p.tkv * D
+    exact = 4.0 * n_sparse * 64 * p.top_k * 64 * D
+    interval = 4.0 * n_sparse * 64 * p.nkv * D
+    return BH * (flat + exact + interval), BH * flat, BH * (exact + interval)
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = "uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, device):
+        self.uuid = None
+        try:
+            self.uuid = str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:  # noqa: BLE001
+            pass
+        self.rows, self.proc, self.thread = [], None, None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        rows = self.rows
+        if self.uuid:
+            mine = [r for r in rows if self.uuid.replace("GPU-", "") in r[0]]
+            rows = mine or rows
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, val in zip(names, r[5:9]) if val.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# device-resident runner through the stage entry points of the C ABI
+# ---------------------------------------------------------------------------
+class Runner:
+    def __init__(self, q, k, v, t_seq_len):
+        self.lib = _capi.load()
+        B, S, H, D = q.shape
+        self.p = _capi.problem(B, S, H, D, t_seq_len)
+        self.L = _capi.workspace_layout(self.p)
+        self.size = self.lib.icsa_workspace_size(ctypes.byref(self.p))
+        self.ws = torch.empty(self.size, dtype=torch.uint8, device=q.device)
+        self.out = torch.empty_like(q)
+        self.q, self.k, self.v = q, k, v
+
+    def step(self, ev=None):
+        lib, pp, st = self.lib, ctypes.byref(self.p), torch.cuda.current_stream().cuda_stream
+        a = (self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr())
+        if ev is not None:
+            ev[0].record()
+        _capi.check(lib.icsa_pool(pp, *a, self.ws.data_ptr(), self.size, st), "icsa_pool")
+        if ev is not None:
+            ev[1].record()
+        _capi.check(lib.icsa_select(pp, a[1], a[2], self.ws.data_ptr(), self.size, st), "icsa_select")
+        if ev is not None:
+            ev[2].record()
+        _capi.check(lib.icsa_attend(pp, *a, None, self.out.data_ptr(), self.ws.data_ptr(), self.size, st),
+                    "icsa_attend")
+        if ev is not None:
+            ev[3].record()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle port on a bounded sample
+# ---------------------------------------------------------------------------
+def cpu_reference_sample(w, flat_blocks, sparse_blocks, seed_base=0):
+    """Run the CPU restatement for head 0 of workload `w`: pooling, compressed
+    attention, selections and extended KV in full, then `flat_blocks` flat and
+    `sparse_blocks` sparse query blocks.  Returns (scaled ms/call, seconds
+    spent, description)."""
+    from oracle import icsa_oracle as orc
+    torch.set_num_threads(os.cpu_count() or 1)
+    q, k, v = (x.float() for x in synthetic.make_inputs(w, heads=[0], seed_base=seed_base, device="cpu"))
+    t = w.t_seq_len
+    c = orc.Counts.make(w.B, w.S, 1, w.D, t)
+    t0 = time.perf_counter()
+    qm, km, vm = orc.block_means(q), orc.block_means(k), orc.block_means(v)
+    s, P, out_c = orc.compressed_attention(*(x.to(torch.bfloat16).permute(0, 2, 1, 3) for x in (qm, km, vm)))
+    sel = orc.select_desc(orc.incontext_keys(P, c.n_t), c.topK)
+    order = orc.select_desc(orc.sharpness_keys(P, c.n_t, c.k_sparsity), c.NB)
+    nk = orc.extended_kv(k, t, sel)[0, 0].to(torch.bfloat16)
+    nv = orc.extended_kv(v, t, sel)[0, 0].to(torch.bfloat16)
+    qb = q[0, :, 0].to(torch.bfloat16).view(c.NB, 64, w.D)
+    kc = orc.block_sums_bf16(nk[None, :, None])[0, 0]
+    vc = orc.block_sums_bf16(nv[None, :, None])[0, 0]
+    t1 = time.perf_counter()
+    fb = order[0, 0, :flat_blocks]
+    qf = qb[fb].reshape(-1, w.D).float()
+    sc = torch.softmax((qf @ nk.float().t()) / (w.D ** 0.5), dim=-1)
+    _ = (sc @ nv.float()).to(torch.bfloat16)
+    t2 = time.perf_counter()
+    sb = order[0, 0, c.num_flat:c.num_flat + sparse_blocks]
+    qsum = orc.block_sums_bf16(qb[sb].reshape(1, -1, 1, w.D))[0, 0]
+    idx = orc.select_desc(qsum.float() @ kc.float().t(), c.top_k)
+    _ = orc.sparse_kernel(qb[sb], nk, nv, kc, vc, idx, c.nkv)
+    t3 = time.perf_counter()
+    per_head = (t1 - t0) + (t2 - t1) * c.num_flat / max(1, flat_blocks) + (t3 - t2) * c.n_sparse / max(1, sparse_blocks)
+    desc = (f"head 0 of {w.H}: pooling, compressed attention, selections and extended KV in full; "
+            f"{flat_blocks}/{c.num_flat} flat and {sparse_blocks}/{c.n_sparse} sparse query blocks; "
+            f"scaled linearly to all blocks and {w.H} heads (fp32 torch on {torch.get_num_threads()} threads)")
+    return per_head * w.H * 1e3, t3 - t0, desc
+
+
+def run_reference_arm(args, rank):
+    """--impl reference: the CPU restatement of the reference path, timed on
+    the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    w = WORKLOADS[args.workload]
+    fb = sb = 4
+    for _ in range(args.warmup):
+        cpu_reference_sample(w, fb, sb)
+    vals = []
+    for _ in range(args.steps):
+        ms, _, desc = cpu_reference_sample(w, fb, sb)
+        vals.append(ms)
+    value = statistics.mean(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "ms/call", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": value, "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": config_dict(w, args.gpus),
+            "cpu_baseline": {"value": value, "unit": "ms/call", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": value, "unit": "ms/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(w, n):
+    return {"workload": w.name, "B": w.B, "H": w.H, "D": w.D, "S": w.S, "t_seq_len": w.t_seq_len,
+            "grid": list(w.grid), "heads_per_gpu": w.H // n, "parallelism": f"head-sharded x{n}",
+            "sparsity_ratio": 0.0625, "select_ratio": 0.125, "flat_ratio": 0.5,
+            "l2": "inputs (q,k,v) larger than L2; no flush"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="480p", choices=list(WORKLOADS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+
+    import datetime
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    w = WORKLOADS[args.workload]
+    if w.H % world != 0:
+        raise SystemExit(f"{w.H} heads do not split over {world} GPUs")
+    hp = w.H // world
+    heads = list(range(rank * hp, (rank + 1) * hp))
+    q, k, v = synthetic.make_inputs(w, heads=heads, device=dev)
+    runner = Runner(q, k, v, w.t_seq_len)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        runner.step()
+    barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    clocks = ClockSampler(dev)
+    clocks.start()
+    barrier()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for i in range(args.steps):
+        runner.step(evs[i])
+    t_end.record()
+    barrier()
+    clk = clocks.stop()
+    elapsed = t_start.elapsed_time(t_end)
+    stage = {n: statistics.mean(e[i].elapsed_time(e[i + 1]) for e in evs) for i, n in
+             enumerate(("pool", "select", "attend"))}
+    rc = runner.lib.icsa_device_status(runner.ws.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    _capi.check(rc, "icsa_device_status")
+
+    # e2e through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+        hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+        def e2e_step():
+            dq, dk, dv = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
+            o = editing_sparse_attention(dq, dk, dv, w.t_seq_len, w.t_seq_len)
+            hout.copy_(o, non_blocking=True)
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        e2e = {"value": e2e_ms, "unit": "ms/call", "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
+               "d2h_bytes_per_step": q.numel() * q.element_size()}
+
+    ms = elapsed / args.steps
+    att = stage["attend"]
+    if dist is not None:
+        t = torch.tensor([ms, att, e2e["value"] if e2e else 0.0], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, att = float(t[0]), float(t[1])
+        if e2e:
+            e2e["value"] = float(t[2])
+    sustained, burst, hbm, src = peaks()
+    flops, _, _ = attention_flops(runner.p, runner.L.n_sparse)
+    achieved = flops / (att * 1e-3) / 1e12
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "attention_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            tr = json.load(f)
+        if tr.get("workload") == w.name and tr.get("heads") == hp:
+            traffic = tr.get("dram_bytes_per_launch")
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": ms, "unit": "ms/call", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded blurred-field generator)",
+                "config": config_dict(w, world),
+                "stages_ms": stage,
+                "roofline": {"bound": "tensor", "kernel": "attn_kernel (stage 3)", "achieved": achieved,
+                             "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained,
+                             "peak_kind": f"{src} sustained bf16", "frac_of_burst": achieved / burst,
+                             "traffic": traffic, "flops_per_launch": flops},
+                "clocks": clk, "gpu_launches": KERNELS_PER_CALL_ALIGNED * args.steps}
+        if e2e:
+            line["e2e"] = e2e
+        if world == 1 and not args.no_cpu_baseline:
+            cms, secs, desc = cpu_reference_sample(w, 64, 64)
+            line["cpu_baseline"] = {"value": cms, "unit": "ms/call", "cores": torch.get_num_threads(),
+                                    "kind": "port", "sample": desc, "sample_seconds": secs}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,153 @@
+"""GPU parity of the whole call and of each stage against the CPU oracle.
+
+Tolerances (from the project contract):
+* selections (in-context top-K, flat/sparse split, per-block top-k): bit-exact
+  given the GPU's own fp32 keys, ties to the lower index;
+* output in bf16: max-abs <= 2e-2 and mean-abs <= 1e-3.
+"""
+import pytest
+import torch
+
+from in_context_sparse_attention import synthetic
+from oracle import icsa_oracle as orc
+
+from _helpers import errors, gpu_selections, oracle_forced, region, run_gpu
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS_BF16, MEAN_ABS_BF16 = 2e-2, 1e-3
+
+
+def _rand(B, S, H, D, dtype, seed, corr=True, t=None):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, S, H, D, generator=g)
+    k = torch.randn(B, S, H, D, generator=g)
+    v = torch.randn(B, S, H, D, generator=g)
+    if corr and t is not None and 0 < t < S:
+        n = min(t, S - t)
+        k[:, t:t + n] = 0.8 * k[:, :n] + 0.6 * torch.randn(B, n, H, D, generator=g)
+        v[:, t:t + n] = 0.8 * v[:, :n] + 0.6 * torch.randn(B, n, H, D, generator=g)
+    return q.to(dtype), k.to(dtype), v.to(dtype)
+
+
+def _check_selection_exact(sels, c):
+    """The GPU's selections equal the oracle selector applied to the GPU's keys."""
+    if c.topK > 0:
+        assert torch.equal(orc.select_desc(sels["colsum"], c.topK), sels["sel"])
+    assert torch.equal(orc.select_desc(sels["sharp"], c.NB), sels["order"])
+    if c.n_sparse > 0:
+        assert torch.equal(orc.select_desc(sels["blockscore"], c.top_k), sels["sparse_idx"])
+
+
+CASES = {
+    # name: (B, S, H, D, t, dtype, flat_ratio)
+    "cfg1_bf16": (1, 8192, 2, 64, 4096, torch.bfloat16, 0.5),
+    "d128_bf16": (1, 4096, 2, 128, 2048, torch.bfloat16, 0.5),
+    "odd_counts_b2": (2, 64 * 37, 2, 128, 64 * 20, torch.bfloat16, 0.5),
+    "unaligned": (1, 5000, 2, 128, 2500, torch.bfloat16, 0.5),
+    "all_sparse": (1, 4096, 2, 128, 2048, torch.bfloat16, 0.0),
+    "all_flat": (1, 4096, 2, 128, 2048, torch.bfloat16, 1.0),
+}
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_call_matches_oracle(cuda_device, name):
+    B, S, H, D, t, dt, fr = CASES[name]
+    q, k, v = _rand(B, S, H, D, dt, seed=sum(map(ord, name)), t=t)
+    out, dbg = run_gpu(q.cuda(), k.cuda(), v.cuda(), t, flat_ratio=fr)
+    assert out.dtype == dt and out.shape == q.shape
+    assert torch.isfinite(out.float()).all()
+    sels = gpu_selections(dbg)
+    c = orc.Counts.make(B, S, H, D, t, flat_ratio=fr)
+    _check_selection_exact(sels, c)
+    ref = oracle_forced(q, k, v, t, sels, flat_ratio=fr)
+    mx, mn = errors(out, ref.out)
+    print(f"{name}: max|d|={mx:.3e} mean|d|={mn:.3e}")
+    assert mx <= MAX_ABS_BF16 and mn <= MEAN_ABS_BF16
+
+
+def test_keys_match_oracle(cuda_device):
+    """fp32 keys agree with the oracle's (which uses the GPU's selections)."""
+    B, S, H, D, t = 1, 8192, 2, 64, 4096
+    q, k, v = _rand(B, S, H, D, torch.bfloat16, seed=7, t=t)
+    _, dbg = run_gpu(q.cuda(), k.cuda(), v.cuda(), t)
+    sels = gpu_selections(dbg)
+    ref = oracle_forced(q, k, v, t, sels)
+    torch.testing.assert_close(sels["colsum"], ref.colsum.float(), rtol=1e-4, atol=1e-6)
+    torch.testing.assert_close(sels["sharp"], ref.sharp.float(), rtol=1e-4, atol=1e-6)
+    torch.testing.assert_close(sels["outc"], ref.out_c.float(), rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(sels["blockscore"], ref.blockscore.float(), rtol=1e-4, atol=1e-3)
+    # the oracle's own selections from its own keys agree with the GPU's
+    own = orc.editing_sparse_attention(q, k, v, t)
+    assert torch.equal(own.sel, sels["sel"])
+    flat_gpu = sels["order"][..., :own.counts.num_flat].sort(-1).values
+    flat_orc = own.order[..., :own.counts.num_flat].sort(-1).values
+    assert (flat_gpu == flat_orc).float().mean() > 0.98
+
+
+def test_pool_stage(cuda_device):
+    """Block sums (bf16) and means against the oracle, partial last block."""
+    B, S, H, D, t = 1, 64 * 20 + 17, 2, 128, 640
+    for dt in (torch.bfloat16, torch.float32):
+        q, k, v = _rand(B, S, H, D, dt, seed=3, t=t)
+        _, dbg = run_gpu(q.cuda(), k.cuda(), v.cuda(), t)
+        NB = (S + 63) // 64
+        for name, x in (("q", q), ("k", k), ("v", v)):
+            s = region(dbg, name + "sum", torch.bfloat16, (B, H, NB, D)).float().cpu()
+            m = region(dbg, name + "mean", torch.float32, (B, H, NB, D)).cpu()
+            s_ref = orc.block_sums_bf16(x).float()
+            m_ref = orc.block_means(x).float().permute(0, 2, 1, 3)
+            torch.testing.assert_close(s, s_ref, rtol=2 ** -7, atol=1e-3)
+            torch.testing.assert_close(m, m_ref, rtol=2 ** -7 if dt == torch.bfloat16 else 1e-5, atol=1e-5)
+
+
+def test_golden_config1(cuda_device):
+    """BASELINE configuration 1 (fp32) against the reference run recorded in
+    tests/golden/config1_reference.pt."""
+    import os
+    fx = torch.load(os.path.join(os.path.dirname(__file__), "golden", "config1_reference.pt"))
+    w = synthetic.CONFIG1
+    q, k, v = synthetic.make_inputs(w)
+    out, dbg = run_gpu(q.cuda(), k.cuda(), v.cuda(), w.t_seq_len)
+    assert out.dtype == torch.float32
+    sels = gpu_selections(dbg)
+    assert torch.equal(sels["sel"], fx["sel"])
+    c = orc.Counts.make(w.B, w.S, w.H, w.D, w.t_seq_len)
+    flat_gpu = sels["order"][..., :c.num_flat].sort(-1).values
+    flat_ref = fx["order"][..., :c.num_flat].sort(-1).values
+    assert torch.equal(flat_gpu, flat_ref)
+    mx, mn = errors(out[:, ::13], fx["out_rows"])
+    print(f"config1 vs reference: max|d|={mx:.3e} mean|d|={mn:.3e}")
+    assert mx <= MAX_ABS_BF16 and mn <= MEAN_ABS_BF16
+
+
+def test_alpha_tensor_mixed_dtypes(cuda_device):
+    """The DiT call: fp32 q/k, bf16 v, per-token gate alpha [B,S,1,1] fp32."""
+    B, S, H, D, t = 1, 4096, 2, 128, 2048
+    q, k, v = _rand(B, S, H, D, torch.float32, seed=11, t=t)
+    v = v.to(torch.bfloat16)
+    alpha = (torch.rand(B, S, 1, 1, generator=torch.Generator().manual_seed(5)) - 0.5) * 0.5
+    out, dbg = run_gpu(q.cuda(), k.cuda(), v.cuda(), t, alpha=alpha.cuda())
+    assert out.dtype == torch.float32
+    sels = gpu_selections(dbg)
+    ref = oracle_forced(q, k, v, t, sels, alpha=alpha)
+    mx, mn = errors(out, ref.out)
+    print(f"mixed dtypes + alpha tensor: max|d|={mx:.3e} mean|d|={mn:.3e}")
+    assert mx <= MAX_ABS_BF16 and mn <= MEAN_ABS_BF16
+
+
+def test_deterministic(cuda_device):
+    B, S, H, D, t = 1, 4096, 2, 128, 2048
+    q, k, v = (x.cuda() for x in _rand(B, S, H, D, torch.bfloat16, seed=21, t=t))
+    a, _ = run_gpu(q, k, v, t)
+    b, _ = run_gpu(q, k, v, t)
+    assert torch.equal(a, b)
+
+
+def test_device_status_clean(cuda_device):
+    from in_context_sparse_attention import _capi
+    B, S, H, D, t = 1, 4096, 2, 128, 2048
+    q, k, v = (x.cuda() for x in _rand(B, S, H, D, torch.bfloat16, seed=2, t=t))
+    _, dbg = run_gpu(q, k, v, t)
+    rc = _capi.load().icsa_device_status(dbg["workspace"].data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
