@@ -175,6 +175,27 @@ ICSA_API int icsa_attend(const icsa_problem* p, const void* q, const void* k, co
  */
 ICSA_API int icsa_device_status(void* workspace, cudaStream_t stream);
 
+/*
+ * Allocation-free variant of icsa_forward.  This entry point has no
+ * counterpart in the reference; it exists for callers that cannot allocate
+ * device memory where they make the call (a plugin host that owns all
+ * allocations, a runtime with a fixed memory budget, an FFI caller without a
+ * CUDA allocator).  They pass inputs and output only; the scratch is a
+ * 64 MiB array inside the library's device code, which each GPU that loads it
+ * keeps until the process exits (loaded at the first call on that GPU under
+ * the default lazy module loading).  Problems whose icsa_workspace_size()
+ * exceeds icsa_static_scratch_bytes() are rejected with ICSA_ERR_WORKSPACE.
+ * All calls share that one array: calls that overlap on the GPU race, so
+ * order them on one stream.  The first call on each device looks the array's
+ * address up (and may load the module); make it before any stream capture.
+ * No cudaMalloc/cudaFree or other allocating routine is called.
+ */
+ICSA_API int icsa_forward_static(const icsa_problem* p, const void* q, const void* k, const void* v,
+                                 const void* alpha, void* out, cudaStream_t stream);
+
+/* Size in bytes of the static scratch used by icsa_forward_static. */
+ICSA_API size_t icsa_static_scratch_bytes(void);
+
 #ifdef __cplusplus
 }
 #endif

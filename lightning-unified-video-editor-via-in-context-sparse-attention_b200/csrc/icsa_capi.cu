@@ -296,6 +296,8 @@ int run_attend(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, 
 // ===========================================================================
 extern "C" {
 
+void icsa_set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
 const char* icsa_last_error(void) { return g_last_error.c_str(); }
 
 const char* icsa_version(void) { return "icsa-b200 0.1 (sm_100a, tcgen05)"; }

@@ -3,6 +3,10 @@
 
 #include "icsa_common.cuh"
 
+// Sets the message returned by icsa_last_error() on the calling thread
+// (library-internal, defined in icsa_capi.cu).
+extern "C" void icsa_set_last_error(const char* msg);
+
 namespace icsa {
 
 // ---------------------------------------------------------------- stage 1 --
