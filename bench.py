@@ -233,6 +233,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--heads", type=int, default=0, help="run only this many heads (profiling of a small case)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -252,6 +253,9 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     w = WORKLOADS[args.workload]
+    if args.heads:
+        import dataclasses
+        w = dataclasses.replace(w, H=args.heads, name=f"{w.name}_h{args.heads}")
     if w.H % world != 0:
         raise SystemExit(f"{w.H} heads do not split over {world} GPUs")
     hp = w.H // world

@@ -281,6 +281,26 @@ ICSA_DEV bool warp_mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
 // ---------------------------------------------------------------------------
 // Warps 0-3: softmax.  Thread t owns query row t of the tile.
 // ---------------------------------------------------------------------------
+// 2^x on the multi-function unit (flushes subnormal results to zero, which
+// only affects probabilities below 2^-126 of the row maximum).
+ICSA_DEV float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Max / sum over 128 registers with 8 independent chains (a single chain
+// would serialise 128 dependent instructions).
+ICSA_DEV float max128(const float (&s)[128]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = s[i];
+#pragma unroll
+  for (int c = 8; c < 128; ++c) m[c & 7] = fmaxf(m[c & 7], s[c]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[i], m[i + 4]);
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
 ICSA_DEV void tmem_load_row128(uint32_t taddr, float (&s)[128]) {
   uint32_t r[4][32];
 #pragma unroll
@@ -328,7 +348,7 @@ ICSA_DEV void run_softmax(const AttnParams& p, const Tile& t, Smem<D>& sm, uint3
   const float sl2 = p.scale_log2;
   const int words = p.nkv_pad / 32;
   const uint32_t* mask_row =
-      t.sparse ? p.sel_mask + (size_t(t.bh) * p.n_sparse + t.rank[half]) * words : nullptr;
+      t.sparse ? p.sel_mask + (size_t(t.bh) * p.n_sparse + (half ? t.rank[1] : t.rank[0])) * words : nullptr;
   rs.m_ref = -INFINITY;
   rs.m_true = -INFINITY;
   rs.l = 0.f;
@@ -355,10 +375,10 @@ ICSA_DEV void run_softmax(const AttnParams& p, const Tile& t, Smem<D>& sm, uint3
       } else {
         hi = min(128, p.tkv - j * 128);
       }
-      float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 128; ++c)
-        if (c >= lo && c < hi) mx = fmaxf(mx, s[c]);
+        if (c < lo || c >= hi) s[c] = -INFINITY;
+      const float mx = max128(s);
       rs.m_true = fmaxf(rs.m_true, mx);
       need = (mx - rs.m_ref) * sl2 > kRescaleThreshold;
       if (need) {
@@ -367,14 +387,14 @@ ICSA_DEV void run_softmax(const AttnParams& p, const Tile& t, Smem<D>& sm, uint3
         rs.l *= alpha;
       }
       const float neg = -rs.m_ref * sl2;
-      float sum = 0.f;
+      float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 128; ++c) {
-        const float e = (c >= lo && c < hi) ? exp2f(fmaf(s[c], sl2, neg)) : 0.f;
+        const float e = ex2(fmaf(s[c], sl2, neg));  // masked: 2^-inf = 0
         s[c] = e;
-        sum += e;
+        part[c & 7] += e;
       }
-      rs.l += sum;
+      rs.l += ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
     } else {
       // Interval term: two BN=64 chunks of pooled blocks per step.
       const int ci = j - t.n_exact;
@@ -382,7 +402,7 @@ ICSA_DEV void run_softmax(const AttnParams& p, const Tile& t, Smem<D>& sm, uint3
       for (int hh = 0; hh < 2; ++hh) {
         const int chunk = 2 * ci + hh;
         const uint32_t w0 = mask_row[chunk * 2], w1 = mask_row[chunk * 2 + 1];
-        float cm = -INFINITY;
+        float cm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           const int blk = chunk * 64 + c;
@@ -390,19 +410,19 @@ ICSA_DEV void run_softmax(const AttnParams& p, const Tile& t, Smem<D>& sm, uint3
           const bool valid = blk < p.nkv && !((w >> (c & 31)) & 1u);
           const float x = s[hh * 64 + c] * (1.0f / 64.0f);
           s[hh * 64 + c] = valid ? x : -INFINITY;
-          cm = fmaxf(cm, s[hh * 64 + c]);
+          cm[c & 3] = fmaxf(cm[c & 3], s[hh * 64 + c]);
         }
-        rs.m_true = fmaxf(rs.m_true, cm);
+        rs.m_true = fmaxf(rs.m_true, fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3])));
         const float neg = -rs.m_true * sl2;
-        float sum = 0.f;
+        float part[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           const float x = s[hh * 64 + c];
-          const float e = (x == -INFINITY) ? 0.f : exp2f(fmaf(x, sl2, neg));
+          const float e = (x == -INFINITY) ? 0.f : ex2(fmaf(x, sl2, neg));
           s[hh * 64 + c] = e;
-          sum += e;
+          part[c & 3] += e;
         }
-        rs.g_l += sum * 64.0f;
+        rs.g_l += ((part[0] + part[1]) + (part[2] + part[3])) * 64.0f;
       }
     }
 
@@ -452,7 +472,7 @@ ICSA_DEV void run_epilogue(const AttnParams& p, const Tile& t, Smem<D>& sm, uint
   if (!warp_mbar_wait(&sm.pv_done[last & 1], uint32_t(last >> 1) & 1u, p.err, kErrPvDone, abort_flag)) return;
   tc::fence_after_sync();
 
-  const int blk = t.blk[half];
+  const int blk = half ? t.blk[1] : t.blk[0];
   const int token = blk * kBlock + (tid & 63);
   const bool write = (half == 0 || t.write1) && token < p.S;
   float f = 1.f, denom = rs.l;
