@@ -44,7 +44,7 @@ from in_context_sparse_attention import _capi, editing_sparse_attention, synthet
 
 METRIC = "sparse-attn ms/call at 65K joint tokens (40h×128d bf16) 1/2/4/8 GPU; DiT step s"
 WORKLOADS = {"480p": synthetic.WAN480P, "720p": synthetic.WAN720P, "config1": synthetic.CONFIG1}
-KERNELS_PER_CALL_ALIGNED = 10  # pool, scores, rowstats, outc, colsum, 2x sort, extended-KV, top-k, attention
+KERNELS_PER_CALL_ALIGNED = 11  # pool, scores, rowstats, outc, colsum, 2x sort, extended-KV, top-k, dense + sparse attention
 
 
 def peaks():

@@ -25,11 +25,13 @@
 // loads block i of each list and a block-diagonal mask keeps rows 0-63 on the
 // first 64 columns and rows 64-127 on the last 64, so P V is exact for both.
 #include "icsa_kernels.cuh"
-#include "icsa_tcgen05.cuh"
+#include "icsa_attn_common.cuh"
 
 namespace icsa {
 
 namespace {
+
+using namespace attn;
 
 constexpr int kThreads = 192;
 constexpr int kSoftmaxThreads = 128;
@@ -37,16 +39,9 @@ constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256, kColG = 384;
-constexpr int kChunkBytes = 128 * 128;  // one 64-wide K chunk of a 128-row operand
-constexpr float kRescaleThreshold = 8.0f;  // lazy O rescale: p may reach 2^8
 
 enum : int { kStepFlat = 0, kStepExact = 1, kStepInterval = 2 };
 
-// Error codes written to *err (first writer wins).
-enum : int {
-  kErrQ = 0x101, kErrKFull = 0x102, kErrVFull = 0x103, kErrKEmpty = 0x104, kErrVEmpty = 0x105,
-  kErrSFull = 0x106, kErrSEmpty = 0x107, kErrPFull = 0x108, kErrPvDone = 0x109, kErrDrain = 0x10A
-};
 
 template <int D>
 struct Cfg {
@@ -185,18 +180,6 @@ ICSA_DEV void run_producer(const AttnParams& p, const AttnMaps& maps, const Tile
   }
 }
 
-// Bounded wait used when draining at exit: ignores the abort flag so that
-// copies still in flight land before the CTA's shared memory is released.
-ICSA_DEV void drain_wait(uint64_t* bar, uint32_t parity, int* err) {
-  const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_timer_ns() - t0 > 1000000000ull) {
-      report_error(err, kErrDrain);
-      return;
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Warp 5, one thread: tcgen05.mma issuer.
 // ---------------------------------------------------------------------------
@@ -254,64 +237,9 @@ ICSA_DEV void run_mma(const AttnParams& p, const Tile& t, Smem<D>& sm, uint32_t 
   if (t.n_steps > 0) issue_pv<D>(p, t, sm, tmem, t.n_steps - 1);
 }
 
-// Warp-uniform bounded wait: every lane polls the barrier (so each lane
-// acquires the phase), and the decision to give up is taken by the whole warp
-// so that warp-collective tcgen05 instructions stay converged.
-ICSA_DEV bool warp_mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code, volatile int* abort_flag) {
-  bool done = mbar_try_wait(bar, parity);
-  uint64_t t0 = 0;
-  uint32_t it = 0;
-  while (!__all_sync(0xffffffffu, done)) {
-    if (!done) done = mbar_try_wait(bar, parity);
-    bool give_up = *abort_flag != 0;
-    if ((threadIdx.x & 31) == 0 && (++it & 63u) == 0u) {
-      const uint64_t now = global_timer_ns();
-      if (t0 == 0) t0 = now;
-      else if (now - t0 > 1000000000ull) {
-        report_error(err, code);
-        *abort_flag = 1;
-        give_up = true;
-      }
-    }
-    if (__any_sync(0xffffffffu, give_up)) return false;
-  }
-  return true;
-}
-
 // ---------------------------------------------------------------------------
 // Warps 0-3: softmax.  Thread t owns query row t of the tile.
 // ---------------------------------------------------------------------------
-// 2^x on the multi-function unit (flushes subnormal results to zero, which
-// only affects probabilities below 2^-126 of the row maximum).
-ICSA_DEV float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// Max / sum over 128 registers with 8 independent chains (a single chain
-// would serialise 128 dependent instructions).
-ICSA_DEV float max128(const float (&s)[128]) {
-  float m[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m[i] = s[i];
-#pragma unroll
-  for (int c = 8; c < 128; ++c) m[c & 7] = fmaxf(m[c & 7], s[c]);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[i], m[i + 4]);
-  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
-}
-ICSA_DEV void tmem_load_row128(uint32_t taddr, float (&s)[128]) {
-  uint32_t r[4][32];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) tc::tmem_ld32(taddr + c * 32, r[c]);
-  tc::tmem_wait_ld();
-#pragma unroll
-  for (int c = 0; c < 4; ++c)
-#pragma unroll
-    for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[c][e]);
-}
-
 // Store one row of P (128 bf16) into the SW128 K-major P tile: two 64-wide
 // chunks of [128 rows][128 B]; 16-byte piece i of row r sits at slot i ^ (r & 7).
 ICSA_DEV void store_p_row(uint8_t* ptile, int row, const float (&pr)[128]) {
@@ -454,13 +382,6 @@ ICSA_DEV void run_softmax(const AttnParams& p, const Tile& t, Smem<D>& sm, uint3
 // Epilogue: normalise, round to bf16 as the reference's attention outputs
 // are, add the compressed-attention residual and store the row in place.
 // ---------------------------------------------------------------------------
-ICSA_DEV float load_alpha(const AttnParams& p, int b, int token, int h, int d) {
-  const long long off = b * p.alpha_strides[0] + token * p.alpha_strides[1] + h * p.alpha_strides[2] +
-                        d * p.alpha_strides[3];
-  if (p.alpha_dtype == ICSA_F32) return reinterpret_cast<const float*>(p.alpha)[off];
-  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.alpha)[off]);
-}
-
 template <int D>
 ICSA_DEV void run_epilogue(const AttnParams& p, const Tile& t, Smem<D>& sm, uint32_t tmem, const RowState& rs) {
   volatile int* abort_flag = &sm.abort_flag;
@@ -489,39 +410,14 @@ ICSA_DEV void run_epilogue(const AttnParams& p, const Tile& t, Smem<D>& sm, uint
     tc::tmem_ld32(tmem + lane_base + kColO + c * 32, ro);
     if (t.sparse) tc::tmem_ld32(tmem + lane_base + kColG + c * 32, rg);
     tc::tmem_wait_ld();
-    float x[32];
+    float o[32];
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
       float acc = __uint_as_float(ro[e]);
       if (t.sparse) acc = acc * f + __uint_as_float(rg[e]);
-      const float o = bf16_round(denom == 0.f ? 0.f : __fdiv_rn(acc, denom));
-      const int d = c * 32 + e;
-      float cval = oc[d];
-      if (p.outc_bf16) cval = bf16_round(cval);
-      const float a = (p.alpha_mode == ICSA_ALPHA_SCALAR) ? p.alpha_scalar : load_alpha(p, t.b, token, t.h, d);
-      float ca = cval * a;
-      if (p.ca_bf16) ca = bf16_round(ca);
-      x[e] = o + ca;
+      o[e] = denom == 0.f ? 0.f : __fdiv_rn(acc, denom);
     }
-    if (!write) {
-      // nothing to store for duplicated or padding rows
-    } else if (p.out_dtype == ICSA_BF16) {
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + out_row + c * 32;
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        uint4 u;
-        u.x = pack_bf16x2(x[v * 8 + 0], x[v * 8 + 1]);
-        u.y = pack_bf16x2(x[v * 8 + 2], x[v * 8 + 3]);
-        u.z = pack_bf16x2(x[v * 8 + 4], x[v * 8 + 5]);
-        u.w = pack_bf16x2(x[v * 8 + 6], x[v * 8 + 7]);
-        reinterpret_cast<uint4*>(dst)[v] = u;
-      }
-    } else {
-      float* dst = reinterpret_cast<float*>(p.out) + out_row + c * 32;
-#pragma unroll
-      for (int v = 0; v < 8; ++v)
-        reinterpret_cast<float4*>(dst)[v] = make_float4(x[v * 4], x[v * 4 + 1], x[v * 4 + 2], x[v * 4 + 3]);
-    }
+    if (write) store_out32(p, t.b, token, t.h, oc, c * 32, o, out_row);
   }
 }
 

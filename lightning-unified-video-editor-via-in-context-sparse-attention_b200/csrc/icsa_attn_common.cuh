@@ -1,0 +1,152 @@
+// Device helpers shared by the attention kernels (dense "flat" tiles and
+// block-sparse tiles).
+#pragma once
+
+#include "icsa_kernels.cuh"
+#include "icsa_tcgen05.cuh"
+
+namespace icsa {
+namespace attn {
+
+constexpr int kChunkBytes = 128 * 128;     // one 64-wide K chunk of a 128-row operand (SW128)
+constexpr float kRescaleThreshold = 8.0f;  // lazy O rescale: p may reach 2^8
+
+// Error codes written to *err (first writer wins).
+enum : int {
+  kErrQ = 0x101, kErrKFull = 0x102, kErrVFull = 0x103, kErrKEmpty = 0x104, kErrVEmpty = 0x105,
+  kErrSFull = 0x106, kErrSEmpty = 0x107, kErrPFull = 0x108, kErrPvDone = 0x109, kErrDrain = 0x10A
+};
+
+// Warp-uniform bounded wait: every lane polls the barrier (so each lane
+// acquires the phase), and the decision to give up is taken by the whole warp
+// so that warp-collective tcgen05 instructions stay converged.
+ICSA_DEV bool warp_mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code, volatile int* abort_flag) {
+  bool done = mbar_try_wait(bar, parity);
+  uint64_t t0 = 0;
+  uint32_t it = 0;
+  while (!__all_sync(0xffffffffu, done)) {
+    if (!done) done = mbar_try_wait(bar, parity);
+    bool give_up = *abort_flag != 0;
+    if ((threadIdx.x & 31) == 0 && (++it & 63u) == 0u) {
+      const uint64_t now = global_timer_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > 1000000000ull) {
+        report_error(err, code);
+        *abort_flag = 1;
+        give_up = true;
+      }
+    }
+    if (__any_sync(0xffffffffu, give_up)) return false;
+  }
+  return true;
+}
+
+// Bounded wait used when draining at exit: ignores the abort flag so that
+// copies still in flight land before the CTA's shared memory is released.
+ICSA_DEV void drain_wait(uint64_t* bar, uint32_t parity, int* err) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > 1000000000ull) {
+      report_error(err, kErrDrain);
+      return;
+    }
+  }
+}
+
+// 2^x on the multi-function unit (flushes subnormal results to zero, which
+// only affects probabilities below 2^-126 of the row maximum).
+ICSA_DEV float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Max / sum over 128 registers with 8 independent chains (a single chain
+// would serialise 128 dependent instructions).
+ICSA_DEV float max128(const float (&s)[128]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = s[i];
+#pragma unroll
+  for (int c = 8; c < 128; ++c) m[c & 7] = fmaxf(m[c & 7], s[c]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[i], m[i + 4]);
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+ICSA_DEV void tmem_load_row128(uint32_t taddr, float (&s)[128]) {
+  uint32_t r[4][32];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) tc::tmem_ld32(taddr + c * 32, r[c]);
+  tc::tmem_wait_ld();
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[c][e]);
+}
+
+ICSA_DEV float load_alpha(const AttnParams& p, int b, int token, int h, int d) {
+  const long long off = b * p.alpha_strides[0] + token * p.alpha_strides[1] + h * p.alpha_strides[2] +
+                        d * p.alpha_strides[3];
+  if (p.alpha_dtype == ICSA_F32) return reinterpret_cast<const float*>(p.alpha)[off];
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.alpha)[off]);
+}
+
+
+// Residual epilogue for 32 consecutive features [d0, d0+32) of one output
+// row: x = bf16(o) + out_c * alpha, with the reference's dtype rounding
+// (attention outputs are bf16; out_compress and out_compress*alpha are bf16
+// when the reference computes them in bf16), stored as the output dtype.
+ICSA_DEV void store_out32(const AttnParams& p, int b, int token, int h, const float* oc_row, int d0,
+                          const float (&o)[32], size_t out_row) {
+  float x[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    const int d = d0 + e;
+    float cval = oc_row[d];
+    if (p.outc_bf16) cval = bf16_round(cval);
+    const float a = (p.alpha_mode == ICSA_ALPHA_SCALAR) ? p.alpha_scalar : load_alpha(p, b, token, h, d);
+    float ca = cval * a;
+    if (p.ca_bf16) ca = bf16_round(ca);
+    x[e] = bf16_round(o[e]) + ca;
+  }
+  if (p.out_dtype == ICSA_BF16) {
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + out_row + d0;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      uint4 u;
+      u.x = pack_bf16x2(x[v * 8 + 0], x[v * 8 + 1]);
+      u.y = pack_bf16x2(x[v * 8 + 2], x[v * 8 + 3]);
+      u.z = pack_bf16x2(x[v * 8 + 4], x[v * 8 + 5]);
+      u.w = pack_bf16x2(x[v * 8 + 6], x[v * 8 + 7]);
+      reinterpret_cast<uint4*>(dst)[v] = u;
+    }
+  } else {
+    float* dst = reinterpret_cast<float*>(p.out) + out_row + d0;
+#pragma unroll
+    for (int v = 0; v < 8; ++v)
+      reinterpret_cast<float4*>(dst)[v] = make_float4(x[v * 4], x[v * 4 + 1], x[v * 4 + 2], x[v * 4 + 3]);
+  }
+}
+
+// Packed two-lane fp32 arithmetic (sm_100 f32x2 instructions).
+ICSA_DEV void ffma2(float& x, float& y, float a0, float a1, float b0, float b1, float c0, float c1) {
+  asm("{.reg .b64 a, b, c, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+      "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;}"
+      : "=f"(x), "=f"(y)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+ICSA_DEV void fadd2(float& x, float& y, float a0, float a1, float b0, float b1) {
+  asm("{.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;}"
+      : "=f"(x), "=f"(y)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+ICSA_DEV void fmul2(float& x, float& y, float a0, float a1, float b0, float b1) {
+  asm("{.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;}"
+      : "=f"(x), "=f"(y)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+}  // namespace attn
+}  // namespace icsa

@@ -100,6 +100,9 @@ struct AttnMaps {
   CUtensorMap vc;
 };
 
+// Block-sparse tiles (and, when flat_tiles > 0, single-tile dense tiles).
 cudaError_t launch_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
+// Dense tiles of the flat query blocks, two 128-row tiles per CTA.
+cudaError_t launch_flat_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
 
 }  // namespace icsa

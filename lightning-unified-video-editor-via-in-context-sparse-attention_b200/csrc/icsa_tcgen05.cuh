@@ -60,6 +60,18 @@ ICSA_DEV void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T.  A (M=128 x K=16 bf16 per instruction)
+// sits in 8 consecutive TMEM columns, lane = row, two bf16 per 32-bit column
+// (element 2c in the low half of column c).
+ICSA_DEV void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive (once) on an mbarrier when all previously issued tcgen05.mma of this
 // thread have completed.
 ICSA_DEV void mma_commit(uint64_t* bar) {
@@ -95,6 +107,12 @@ ICSA_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 
 ICSA_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 ICSA_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Per-warp register budget changes (all threads of the warp execute these).
+template <uint32_t N>
+ICSA_DEV void reg_alloc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <uint32_t N>
+ICSA_DEV void reg_dealloc() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
 
 }  // namespace tc
 }  // namespace icsa
