@@ -287,9 +287,7 @@ int run_attend(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, 
   a.err = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + L.err);
   cudaError_t e = icsa::launch_flat_attention(a, maps, p->D, stream);
   if (e != cudaSuccess) return cuda_fail(e, "dense attention");
-  icsa::AttnParams sparse_only = a;
-  sparse_only.flat_tiles = 0;
-  e = icsa::launch_attention(sparse_only, maps, p->D, stream);
+  e = icsa::launch_sparse_attention(a, maps, p->D, stream);
   return e == cudaSuccess ? ICSA_OK : cuda_fail(e, "sparse attention");
 }
 

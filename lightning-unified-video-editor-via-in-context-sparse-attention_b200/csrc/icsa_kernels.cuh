@@ -104,5 +104,7 @@ struct AttnMaps {
 cudaError_t launch_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
 // Dense tiles of the flat query blocks, two 128-row tiles per CTA.
 cudaError_t launch_flat_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
+// Block-sparse tiles (exact top_k blocks + interval term), P kept in TMEM.
+cudaError_t launch_sparse_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
 
 }  // namespace icsa

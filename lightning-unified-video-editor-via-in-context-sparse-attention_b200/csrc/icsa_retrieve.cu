@@ -110,68 +110,99 @@ __global__ void gather_extended_kernel(SelectParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// Per sparse query block: scores against all extended-KV block sums and the
-// top_k selection.  One warp per query block, `warps` blocks of one (b,h)
-// per CTA; KC is staged through shared memory 64 rows at a time.
+// Per sparse query block: fp32 scores QC . KC^T against every extended-KV
+// block (tilelang_host.py:172), then the top_k blocks (:173) by a warp radix
+// select; ties go to the lower block index, and the selected set is written
+// in increasing block order together with its bit set.
+//
+// CTA: `rows` (<= 8) sparse query blocks of one (b,h), 256 threads.  Scoring:
+// thread <-> extended-KV block, 8 query rows register-blocked, the query sums
+// transposed in shared memory ([D][8]) so each k value feeds 8 FMAs.
+// Selection: warp w <-> query block w.
 // ---------------------------------------------------------------------------
-constexpr int kKcChunk = 64;
+constexpr int kTopkThreads = 256;
+constexpr int kTopkRowsMax = 8;
 
-__global__ void sparse_topk_kernel(SelectParams p, int warps, int pow2) {
+__global__ void __launch_bounds__(kTopkThreads) sparse_topk_kernel(SelectParams p, int rows) {
   extern __shared__ __align__(16) unsigned char sh_raw[];
-  const int D = p.D;
-  uint64_t* keys = reinterpret_cast<uint64_t*>(sh_raw);                  // [warps][pow2]
-  float* qrow = reinterpret_cast<float*>(keys + size_t(warps) * pow2);  // [warps][D]
-  float* kct = qrow + size_t(warps) * D;                                 // [64][D+1]
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int D = p.D, nkv = p.nkv;
+  float* qT = reinterpret_cast<float*>(sh_raw);                                  // [D][8]
+  uint32_t* keys = reinterpret_cast<uint32_t*>(qT + D * kTopkRowsMax);           // [rows][nkv]
+  uint32_t* hist = keys + size_t(rows) * nkv;                                    // [8][256]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y;
-  const int r = blockIdx.x * warps + warp;  // sparse query block rank
-  const bool active = r < p.n_sparse;
-  if (active) {
-    const int blk = p.order[size_t(bh) * p.NB + p.num_flat + r];
-    const __nv_bfloat16* qs = p.qsum + (size_t(bh) * p.NB + blk) * D;
-    for (int d = lane; d < D; d += 32) qrow[warp * D + d] = __bfloat162float(qs[d]);
+  const int r0 = blockIdx.x * rows;
+  const int* order = p.order + size_t(bh) * p.NB + p.num_flat;
+  for (int e = tid; e < kTopkRowsMax * D; e += kTopkThreads) {
+    const int r = e / D, d = e % D;
+    float v = 0.f;
+    if (r < rows && r0 + r < p.n_sparse)
+      v = __bfloat162float(p.qsum[(size_t(bh) * p.NB + order[r0 + r]) * D + d]);
+    qT[d * kTopkRowsMax + r] = v;
   }
-  uint64_t* mykeys = keys + size_t(warp) * pow2;
-  for (int j = lane; j < pow2; j += 32) mykeys[j] = 0ull;
+  __syncthreads();
   const __nv_bfloat16* KC = p.kc + size_t(bh) * p.nkv_pad * D;
-  for (int c0 = 0; c0 < p.nkv; c0 += kKcChunk) {
-    __syncthreads();
-    for (int e = threadIdx.x; e < kKcChunk * D; e += blockDim.x) {
-      const int rr = e / D, d = e % D;
-      kct[rr * (D + 1) + d] = (c0 + rr < p.nkv) ? __bfloat162float(KC[size_t(c0 + rr) * D + d]) : 0.f;
-    }
-    __syncthreads();
-    if (active) {
+  for (int col = tid; col < nkv; col += kTopkThreads) {
+    float acc[kTopkRowsMax];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int cc = lane + 32 * half;
-        const int col = c0 + cc;
-        if (col < p.nkv) {
-          float acc = 0.f;
-          const float* kr = kct + cc * (D + 1);
-          const float* qr = qrow + warp * D;
-          for (int d = 0; d < D; ++d) acc = fmaf(qr[d], kr[d], acc);
-          mykeys[col] = select_key(acc, uint32_t(col));
-          if (p.blockscore != nullptr) p.blockscore[(size_t(bh) * p.n_sparse + r) * p.nkv + col] = acc;
-        }
+    for (int r = 0; r < kTopkRowsMax; ++r) acc[r] = 0.f;
+    const __nv_bfloat16* kr = KC + size_t(col) * D;
+    for (int d0 = 0; d0 < D; d0 += 8) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(kr + d0));
+      const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&u);
+      float kf[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(hv[i]);
+        kf[2 * i] = f.x;
+        kf[2 * i + 1] = f.y;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float4 a = reinterpret_cast<const float4*>(qT)[(d0 + e) * 2];
+        const float4 b = reinterpret_cast<const float4*>(qT)[(d0 + e) * 2 + 1];
+        acc[0] = fmaf(a.x, kf[e], acc[0]);
+        acc[1] = fmaf(a.y, kf[e], acc[1]);
+        acc[2] = fmaf(a.z, kf[e], acc[2]);
+        acc[3] = fmaf(a.w, kf[e], acc[3]);
+        acc[4] = fmaf(b.x, kf[e], acc[4]);
+        acc[5] = fmaf(b.y, kf[e], acc[5]);
+        acc[6] = fmaf(b.z, kf[e], acc[6]);
+        acc[7] = fmaf(b.w, kf[e], acc[7]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kTopkRowsMax; ++r) {
+      if (r < rows) {
+        keys[size_t(r) * nkv + col] = float_order_key(acc[r]);
+        if (p.blockscore != nullptr && r0 + r < p.n_sparse)
+          p.blockscore[(size_t(bh) * p.n_sparse + r0 + r) * nkv + col] = acc[r];
       }
     }
   }
-  __syncwarp();
-  if (!active) return;
-  bitonic_sort_desc(mykeys, pow2, lane, 32, WarpSync{});
+  __syncthreads();
+  if (warp >= rows || r0 + warp >= p.n_sparse) return;
+  const int r = r0 + warp;
+  const uint32_t* myk = keys + size_t(warp) * nkv;
+  int n_gt = 0;
+  const uint32_t kth = warp_kth_largest(myk, nkv, p.top_k, hist + warp * 256, &n_gt);
+  const int need_eq = p.top_k - n_gt;
   int* idx = p.sparse_idx + (size_t(bh) * p.n_sparse + r) * p.top_k;
-  for (int i = lane; i < p.top_k; i += 32) idx[i] = int(select_key_index(mykeys[i]));
-  // bit set of the selected blocks, one 32-bit word per lane step
-  const int words = p.nkv_pad / 32;
-  uint32_t* mask = p.sel_mask + (size_t(bh) * p.n_sparse + r) * words;
-  for (int w = lane; w < words; w += 32) {
-    uint32_t bits = 0;
-    for (int i = 0; i < p.top_k; ++i) {
-      const uint32_t sel = select_key_index(mykeys[i]);
-      if (sel / 32 == uint32_t(w)) bits |= 1u << (sel % 32);
-    }
-    mask[w] = bits;
+  uint32_t* mask = p.sel_mask + (size_t(bh) * p.n_sparse + r) * (p.nkv_pad / 32);
+  const uint32_t lt = (1u << lane) - 1u;
+  int written = 0, eq_seen = 0;
+  for (int c0 = 0; c0 < p.nkv_pad; c0 += 32) {
+    const int col = c0 + lane;
+    const uint32_t u = col < nkv ? myk[col] : 0u;
+    const bool gt = col < nkv && u > kth;
+    const bool eq = col < nkv && u == kth;
+    const uint32_t eqm = __ballot_sync(0xffffffffu, eq);
+    const bool take = gt || (eq && eq_seen + __popc(eqm & lt) < need_eq);
+    const uint32_t selm = __ballot_sync(0xffffffffu, take);
+    if (take) idx[written + __popc(selm & lt)] = col;
+    if (lane == 0) mask[c0 / 32] = selm;
+    written += __popc(selm);
+    eq_seen += __popc(eqm);
   }
 }
 
@@ -201,19 +232,18 @@ cudaError_t launch_extended_kv(const SelectParams& p, cudaStream_t stream) {
 cudaError_t launch_sparse_topk(const SelectParams& p, cudaStream_t stream) {
   if (p.n_sparse == 0) return cudaSuccess;
   const int BH = p.B * p.H;
-  const int pow2 = next_pow2(p.nkv);
-  int warps = 8;
-  auto smem_for = [&](int w) {
-    return size_t(w) * pow2 * sizeof(uint64_t) + size_t(w) * p.D * sizeof(float) +
-           size_t(kKcChunk) * (p.D + 1) * sizeof(float);
+  auto smem_for = [&](int rows) {
+    return size_t(kTopkRowsMax) * p.D * sizeof(float) + size_t(rows) * p.nkv * sizeof(uint32_t) +
+           size_t(kTopkRowsMax) * 256 * sizeof(uint32_t);
   };
-  while (warps > 1 && smem_for(warps) > 160 * 1024) warps >>= 1;
-  const size_t smem = smem_for(warps);
+  int rows = kTopkRowsMax;
+  while (rows > 1 && smem_for(rows) > 200 * 1024) --rows;
+  const size_t smem = smem_for(rows);
   if (smem > 220 * 1024) return cudaErrorInvalidConfiguration;
   cudaError_t e = cudaFuncSetAttribute(sparse_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  dim3 g((p.n_sparse + warps - 1) / warps, BH);
-  sparse_topk_kernel<<<g, warps * 32, smem, stream>>>(p, warps, pow2);
+  dim3 g((p.n_sparse + rows - 1) / rows, BH);
+  sparse_topk_kernel<<<g, kTopkThreads, smem, stream>>>(p, rows);
   return cudaGetLastError();
 }
 

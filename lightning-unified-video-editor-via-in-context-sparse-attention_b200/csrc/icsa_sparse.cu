@@ -1,0 +1,449 @@
+// Block-sparse attention for the "sparse" query blocks: the reference's
+// fused tilelang kernel (tilelang_kernels.py:681-997, driven by
+// tilelang_host.py:121-206), fused with the scatter and residual of
+// editing_sparse_attention.py:217-232.
+//
+// Per query block the reference computes
+//   (a) exact online softmax over its top_k selected 64-row KV blocks;
+//   (b) an "interval" term over all pooled KV blocks in chunks of BN = 64:
+//       logits q.KC/64 (KC = block sums), selected blocks and blocks >= nkv
+//       masked, running max updated per chunk (rescaling acc/l of (a)), and
+//       probabilities weighted x64 accumulated into g_l / g_acc WITHOUT
+//       rescaling when a later chunk raises the max;
+//   (c) out = (acc + g_acc) / (l + g_l), 0 where the denominator is 0.
+//
+// Per CTA: one 128-row tile = two sparse query blocks A (rows 0-63) and B
+// (rows 64-127).  Exact step i loads block i of A's list into KV rows 0-63
+// and block i of B's list into rows 64-127; the score tile is then
+// block-diagonal (rows of A only use columns 0-63, rows of B columns 64-127)
+// and P is written with zeros off the diagonal, so one M=128 x N=128 x K=128
+// P.V computes both.  Interval steps load 128 pooled rows (two BN=64 chunks).
+//
+// Roles: warps 0-3 softmax + epilogue (thread t <-> row t <-> TMEM lane t);
+// warp 4 TMA producer; warp 5 TMEM allocator + MMA issuer.
+// TMEM: S double buffer [0,128) [128,256) (P of a step overwrites the first 64
+// columns of its S buffer), O [256,256+D) for the exact part, G [384,384+D) for
+// the interval part.  The MMA thread issues S(j+1) before P(j).V so the tensor
+// core computes the next scores while the softmax of step j runs.
+#include "icsa_attn_common.cuh"
+
+namespace icsa {
+
+namespace {
+
+using namespace attn;
+
+constexpr int kSThreads = 192;
+constexpr int kSProducerWarp = 4;
+constexpr int kSMmaWarp = 5;
+constexpr uint32_t kSTmemCols = 512;
+constexpr uint32_t kSColO = 256, kSColG = 384;
+
+template <int D>
+struct SCfg {
+  static constexpr int kOpBytes = 128 * D * 2;
+  static constexpr int kChunks = D / 64;
+  static constexpr int kStages = (D == 128) ? 3 : 6;
+};
+
+template <int D>
+struct __align__(1024) SSmem {
+  uint8_t q[SCfg<D>::kOpBytes];
+  uint8_t k[SCfg<D>::kStages][SCfg<D>::kOpBytes];
+  uint8_t v[SCfg<D>::kStages][SCfg<D>::kOpBytes];
+  uint64_t q_full;
+  uint64_t k_full[SCfg<D>::kStages], k_empty[SCfg<D>::kStages];
+  uint64_t v_full[SCfg<D>::kStages], v_empty[SCfg<D>::kStages];
+  uint64_t s_full[2], p_full[2], pv_done;  // p_full per S buffer: the softmax may run one step ahead
+  uint64_t mma_fin;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+static_assert(sizeof(SSmem<128>) + 1024 <= 232448, "sparse kernel shared memory exceeds 227 KB");
+static_assert(sizeof(SSmem<64>) + 1024 <= 232448, "sparse kernel shared memory exceeds 227 KB");
+
+struct STile {
+  int bh, b, h;
+  int blk[2];   // query blocks of rows [0,64) and [64,128)
+  int rank[2];  // their ranks in the sparse list
+  int write1;   // 0 when block B duplicates A (odd count)
+  int n_exact, n_steps;
+};
+
+ICSA_DEV STile decode_sparse_tile(const AttnParams& p, int cta) {
+  STile t;
+  t.bh = cta / p.sparse_tiles;
+  const int pair = cta % p.sparse_tiles;
+  t.b = t.bh / p.H;
+  t.h = t.bh % p.H;
+  t.rank[0] = 2 * pair;
+  t.write1 = 2 * pair + 1 < p.n_sparse;
+  t.rank[1] = t.write1 ? 2 * pair + 1 : 2 * pair;
+  const int* order = p.order + size_t(t.bh) * p.NB + p.num_flat;
+  t.blk[0] = order[t.rank[0]];
+  t.blk[1] = order[t.rank[1]];
+  t.n_exact = p.top_k;
+  t.n_steps = p.top_k + p.nkv_pad / 128;
+  return t;
+}
+
+template <int D>
+ICSA_DEV void sparse_producer(const AttnParams& p, const AttnMaps& maps, const STile& t, SSmem<D>& sm) {
+  using C = SCfg<D>;
+  volatile int* abort_flag = &sm.abort_flag;
+  mbar_arrive_expect_tx(&sm.q_full, C::kOpBytes);
+  for (int c = 0; c < C::kChunks; ++c)
+    for (int half = 0; half < 2; ++half)
+      tma_load_4d(sm.q + c * kChunkBytes + half * (kChunkBytes / 2), &maps.q, &sm.q_full, c * 64, t.h,
+                  t.blk[half] * kBlock, t.b);
+  const int* rows = p.kv_rows + size_t(t.bh) * p.nkv;
+  const int* idx = p.sparse_idx + size_t(t.bh) * p.n_sparse * p.top_k;
+  const int* idx0 = idx + size_t(t.rank[0]) * p.top_k;
+  const int* idx1 = idx + size_t(t.rank[1]) * p.top_k;
+  for (int j = 0; j < t.n_steps; ++j) {
+    const int st = j % C::kStages;
+    const uint32_t ph = (uint32_t(j / C::kStages) & 1u) ^ 1u;
+    const bool exact = j < t.n_exact;
+    int r0 = 0, r1 = 0;
+    if (exact) {
+      r0 = rows[idx0[j]];
+      r1 = rows[idx1[j]];
+    }
+    const int prow = (j - t.n_exact) * 128;  // interval: pooled rows
+    if (!mbar_wait(&sm.k_empty[st], ph, p.err, kErrKEmpty, abort_flag)) return;
+    mbar_arrive_expect_tx(&sm.k_full[st], C::kOpBytes);
+    for (int c = 0; c < C::kChunks; ++c) {
+      uint8_t* dst = sm.k[st] + c * kChunkBytes;
+      if (exact) {
+        tma_load_4d(dst, &maps.k, &sm.k_full[st], c * 64, t.h, r0, t.b);
+        tma_load_4d(dst + kChunkBytes / 2, &maps.k, &sm.k_full[st], c * 64, t.h, r1, t.b);
+      } else {
+        tma_load_3d(dst, &maps.kc, &sm.k_full[st], c * 64, prow, t.bh);
+      }
+    }
+    if (!mbar_wait(&sm.v_empty[st], ph, p.err, kErrVEmpty, abort_flag)) return;
+    mbar_arrive_expect_tx(&sm.v_full[st], C::kOpBytes);
+    for (int c = 0; c < C::kChunks; ++c) {
+      uint8_t* dst = sm.v[st] + c * kChunkBytes;
+      if (exact) {
+        tma_load_4d(dst, &maps.v, &sm.v_full[st], c * 64, t.h, r0, t.b);
+        tma_load_4d(dst + kChunkBytes / 2, &maps.v, &sm.v_full[st], c * 64, t.h, r1, t.b);
+      } else {
+        tma_load_3d(dst, &maps.vc, &sm.v_full[st], c * 64, prow, t.bh);
+      }
+    }
+  }
+}
+
+template <int D>
+ICSA_DEV void sparse_issue_s(SSmem<D>& sm, uint32_t tmem, int j) {
+  constexpr uint32_t idesc = tc::make_idesc_bf16(128, 128, false, false);
+  const uint32_t q_addr = smem_u32(sm.q);
+  const uint32_t k_addr = smem_u32(sm.k[j % SCfg<D>::kStages]);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
+    tc::mma_bf16_ss(tmem + (j & 1) * 128, tc::make_sw128_desc(q_addr + off, 16, 1024),
+                    tc::make_sw128_desc(k_addr + off, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+  }
+}
+
+template <int D>
+ICSA_DEV void sparse_issue_pv(SSmem<D>& sm, uint32_t tmem, int j, uint32_t acc_col, bool accumulate) {
+  constexpr uint32_t idesc = tc::make_idesc_bf16(128, D, false, true);
+  const uint32_t v_addr = smem_u32(sm.v[j % SCfg<D>::kStages]);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    tc::mma_bf16_ts(tmem + acc_col, tmem + (j & 1) * 128 + kk * 8,
+                    tc::make_sw128_desc(v_addr + kk * 16 * 128, kChunkBytes, 1024), idesc,
+                    (accumulate || kk > 0) ? 1u : 0u);
+}
+
+template <int D>
+ICSA_DEV void sparse_mma(const AttnParams& p, const STile& t, SSmem<D>& sm, uint32_t tmem) {
+  using C = SCfg<D>;
+  volatile int* abort_flag = &sm.abort_flag;
+  const int n = t.n_steps;
+  if (!mbar_wait(&sm.q_full, 0, p.err, kErrQ, abort_flag)) return;
+  if (!mbar_wait(&sm.k_full[0], 0, p.err, kErrKFull, abort_flag)) return;
+  tc::fence_after_sync();
+  sparse_issue_s<D>(sm, tmem, 0);
+  tc::mma_commit(&sm.s_full[0]);
+  tc::mma_commit(&sm.k_empty[0]);
+  for (int j = 0; j < n; ++j) {
+    if (j + 1 < n) {
+      // S(j+1) goes to the buffer of P(j-1), whose P.V was issued before
+      const int st = (j + 1) % C::kStages;
+      if (!mbar_wait(&sm.k_full[st], uint32_t((j + 1) / C::kStages) & 1u, p.err, kErrKFull, abort_flag)) return;
+      tc::fence_after_sync();
+      sparse_issue_s<D>(sm, tmem, j + 1);
+      tc::mma_commit(&sm.s_full[(j + 1) & 1]);
+      tc::mma_commit(&sm.k_empty[st]);
+    }
+    const int st = j % C::kStages;
+    if (!mbar_wait(&sm.v_full[st], uint32_t(j / C::kStages) & 1u, p.err, kErrVFull, abort_flag)) return;
+    if (!mbar_wait(&sm.p_full[j & 1], uint32_t(j >> 1) & 1u, p.err, kErrPFull, abort_flag)) return;
+    tc::fence_after_sync();
+    const bool interval = j >= t.n_exact;
+    sparse_issue_pv<D>(sm, tmem, j, interval ? kSColG : kSColO, interval ? (j > t.n_exact) : (j > 0));
+    tc::mma_commit(&sm.pv_done);
+    tc::mma_commit(&sm.v_empty[st]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Softmax (warps 0-3) and epilogue.  Warps 0-1 hold the rows of block A,
+// warps 2-3 those of block B, so the block-diagonal half a row needs is
+// warp-uniform.
+// ---------------------------------------------------------------------------
+ICSA_DEV float max64(const float (&s)[64]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = s[i];
+#pragma unroll
+  for (int c = 8; c < 64; ++c) m[c & 7] = fmaxf(m[c & 7], s[c]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[i], m[i + 4]);
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
+template <int D>
+ICSA_DEV void sparse_softmax(const AttnParams& p, const STile& t, SSmem<D>& sm, uint32_t tmem) {
+  volatile int* abort_flag = &sm.abort_flag;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int half = warp >> 1;
+  const uint32_t lanes = uint32_t(warp * 32) << 16;
+  const float sl2 = p.scale_log2;
+  const int n = t.n_steps;
+  const int words = p.nkv_pad / 32;
+  const uint32_t* mask_row = p.sel_mask + (size_t(t.bh) * p.n_sparse + (half ? t.rank[1] : t.rank[0])) * words;
+  float m_ref = -INFINITY;   // exponent origin of O and l (raw score units)
+  float m_true = -INFINITY;  // running max as the reference tracks it
+  float l = 0.f, g_l = 0.f;
+
+  for (int j = 0; j < n; ++j) {
+    const int sb = j & 1;
+    if (!warp_mbar_wait(&sm.s_full[sb], uint32_t(j >> 1) & 1u, p.err, kErrSFull, abort_flag)) return;
+    tc::fence_after_sync();
+    const uint32_t s_col = tmem + lanes + sb * 128;
+    if (j < t.n_exact) {
+      // exact step: this row's 64 keys are columns [64*half, 64*half+64)
+      float s[64];
+      {
+        uint32_t r[2][32];
+        tc::tmem_ld32(s_col + half * 64, r[0]);
+        tc::tmem_ld32(s_col + half * 64 + 32, r[1]);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 64; ++c) s[c] = __uint_as_float(r[c >> 5][c & 31]);
+      }
+      const float mx = max64(s);
+      m_true = fmaxf(m_true, mx);
+      const bool need = (mx - m_ref) * sl2 > kRescaleThreshold;
+      float alpha = 1.f;
+      if (need) {
+        alpha = ex2((m_ref - m_true) * sl2);
+        m_ref = m_true;
+        l *= alpha;
+      }
+      const float neg = -m_ref * sl2;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; c += 4) {
+        ffma2(s[c], s[c + 1], s[c], s[c + 1], sl2, sl2, neg, neg);
+        ffma2(s[c + 2], s[c + 3], s[c + 2], s[c + 3], sl2, sl2, neg, neg);
+        s[c] = ex2(s[c]);
+        s[c + 1] = ex2(s[c + 1]);
+        s[c + 2] = ex2(s[c + 2]);
+        s[c + 3] = ex2(s[c + 3]);
+        fadd2(a0, a1, a0, a1, s[c], s[c + 1]);
+        fadd2(a2, a3, a2, a3, s[c + 2], s[c + 3]);
+      }
+      l += (a0 + a1) + (a2 + a3);
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        if (!warp_mbar_wait(&sm.pv_done, uint32_t(j - 1) & 1u, p.err, kErrPvDone, abort_flag)) return;
+        tc::fence_after_sync();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tc::tmem_ld32(tmem + lanes + kSColO + c * 32, r);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+          tc::tmem_st32(tmem + lanes + kSColO + c * 32, r);
+        }
+      }
+      uint32_t pk[32], zero[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        pk[e] = pack_bf16x2(s[2 * e], s[2 * e + 1]);
+        zero[e] = 0u;
+      }
+      tc::tmem_st32(s_col + half * 32, pk);
+      tc::tmem_st32(s_col + (1 - half) * 32, zero);
+    } else {
+      // interval step: two BN=64 chunks of pooled blocks, all 128 columns
+      float s[128];
+      tmem_load_row128(s_col, s);
+      const int ci = j - t.n_exact;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int chunk = 2 * ci + hh;
+        const uint32_t w0 = mask_row[2 * chunk], w1 = mask_row[2 * chunk + 1];
+        float cm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const uint32_t w = c < 32 ? w0 : w1;
+          const bool valid = chunk * 64 + c < p.nkv && !((w >> (c & 31)) & 1u);
+          const float x = valid ? s[hh * 64 + c] * (1.0f / 64.0f) : -INFINITY;
+          s[hh * 64 + c] = x;
+          cm[c & 3] = fmaxf(cm[c & 3], x);
+        }
+        m_true = fmaxf(m_true, fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3])));
+        const float neg = -m_true * sl2;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 64; c += 4) {
+          float* x = s + hh * 64 + c;
+          ffma2(x[0], x[1], x[0], x[1], sl2, sl2, neg, neg);
+          ffma2(x[2], x[3], x[2], x[3], sl2, sl2, neg, neg);
+          x[0] = ex2(x[0]);
+          x[1] = ex2(x[1]);
+          x[2] = ex2(x[2]);
+          x[3] = ex2(x[3]);
+          fadd2(a0, a1, a0, a1, x[0], x[1]);
+          fadd2(a2, a3, a2, a3, x[2], x[3]);
+        }
+        g_l += ((a0 + a1) + (a2 + a3)) * 64.0f;
+      }
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pk[e] = pack_bf16x2(s[h2 * 64 + 2 * e], s[h2 * 64 + 2 * e + 1]);
+        tc::tmem_st32(s_col + h2 * 32, pk);
+      }
+    }
+    tc::tmem_wait_st();
+    tc::fence_before_sync();
+    mbar_arrive(&sm.p_full[j & 1]);
+  }
+
+  // epilogue: (acc * f + g_acc) / (l * f + g_l), f re-bases acc and l on the final max
+  if (!warp_mbar_wait(&sm.pv_done, uint32_t(n - 1) & 1u, p.err, kErrPvDone, abort_flag)) return;
+  tc::fence_after_sync();
+  const float f = ex2((m_ref - m_true) * sl2);
+  const float denom = l * f + g_l;
+  const int blk = half ? t.blk[1] : t.blk[0];
+  const int token = blk * kBlock + (tid & 63);
+  const bool write = (half == 0 || t.write1) && token < p.S;
+  const float* oc = p.outc + (size_t(t.bh) * p.NB + blk) * D;
+  const size_t out_row = ((size_t(t.b) * p.S + token) * p.H + t.h) * D;
+#pragma unroll 1
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t ro[32], rg[32];
+    __syncwarp();
+    tc::tmem_ld32(tmem + lanes + kSColO + c * 32, ro);
+    tc::tmem_ld32(tmem + lanes + kSColG + c * 32, rg);
+    tc::tmem_wait_ld();
+    float o[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const float acc = fmaf(__uint_as_float(ro[e]), f, __uint_as_float(rg[e]));
+      o[e] = denom == 0.f ? 0.f : __fdiv_rn(acc, denom);
+    }
+    if (write) store_out32(p, t.b, token, t.h, oc, c * 32, o, out_row);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kSThreads, 1) sparse_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps) {
+  extern __shared__ uint8_t smem_raw[];
+  SSmem<D>& sm = *reinterpret_cast<SSmem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using C = SCfg<D>;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const STile t = decode_sparse_tile(p, blockIdx.x);
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(&sm.k_full[i], 1);
+      mbar_init(&sm.k_empty[i], 1);
+      mbar_init(&sm.v_full[i], 1);
+      mbar_init(&sm.v_empty[i], 1);
+    }
+    mbar_init(&sm.s_full[0], 1);
+    mbar_init(&sm.s_full[1], 1);
+    mbar_init(&sm.p_full[0], 128);
+    mbar_init(&sm.p_full[1], 128);
+    mbar_init(&sm.pv_done, 1);
+    mbar_init(&sm.mma_fin, 1);
+    sm.abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == kSMmaWarp) {
+    tc::tmem_alloc(&sm.tmem_base, kSTmemCols);
+    tc::tmem_relinquish();
+  }
+  if (warp == kSProducerWarp && lane == 0) {
+    prefetch_tensormap(&maps.q);
+    prefetch_tensormap(&maps.k);
+    prefetch_tensormap(&maps.v);
+    prefetch_tensormap(&maps.kc);
+    prefetch_tensormap(&maps.vc);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  if (warp < 4) {
+    sparse_softmax<D>(p, t, sm, tmem);
+  } else if (warp == kSProducerWarp) {
+    if (lane == 0) {
+      sparse_producer<D>(p, maps, t, sm);
+      if (sm.abort_flag) {
+        for (int j = max(0, t.n_steps - C::kStages); j < t.n_steps; ++j) {
+          drain_wait(&sm.k_full[j % C::kStages], uint32_t(j / C::kStages) & 1u, p.err);
+          drain_wait(&sm.v_full[j % C::kStages], uint32_t(j / C::kStages) & 1u, p.err);
+        }
+        drain_wait(&sm.q_full, 0, p.err);
+      }
+    }
+  } else {
+    if (lane == 0) {
+      sparse_mma<D>(p, t, sm, tmem);
+      tc::mma_commit(&sm.mma_fin);
+      drain_wait(&sm.mma_fin, 0, p.err);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == kSMmaWarp) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kSTmemCols);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_sparse_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream) {
+  const int ctas = p.B * p.H * p.sparse_tiles;
+  if (ctas == 0) return cudaSuccess;
+  if (D == 128) {
+    const size_t smem = sizeof(SSmem<128>) + 1024;
+    cudaError_t e = cudaFuncSetAttribute(sparse_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    sparse_kernel<128><<<ctas, kSThreads, smem, stream>>>(p, maps);
+  } else if (D == 64) {
+    const size_t smem = sizeof(SSmem<64>) + 1024;
+    cudaError_t e = cudaFuncSetAttribute(sparse_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    sparse_kernel<64><<<ctas, kSThreads, smem, stream>>>(p, maps);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace icsa
