@@ -10,7 +10,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#include "../../include/icsa.h"
+#include "icsa.h"
 
 #define ICSA_DEV __device__ __forceinline__
 

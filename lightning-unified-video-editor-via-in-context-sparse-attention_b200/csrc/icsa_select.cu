@@ -71,11 +71,16 @@ __global__ void __launch_bounds__(256) scores_kernel(SelectParams p) {
 
 // ---------------------------------------------------------------------------
 // Per row: softmax statistics and the sharpness key.  One warp per row; the
-// target-column scores are bitonic-sorted in shared memory and the
-// k_sparsity largest probabilities are summed in descending order.
+// k_sparsity-th largest target-column score is found by a radix select over
+// order-preserving keys, and the sharpness is the sum of the probabilities
+// above it plus the remaining ties at it (the sum of the k_sparsity largest).
 // ---------------------------------------------------------------------------
-__global__ void rowstats_kernel(SelectParams p, int pow2_t, int warps) {
-  extern __shared__ float sh_rows[];
+ICSA_DEV float order_key_to_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+__global__ void rowstats_kernel(SelectParams p, int warps, int stride) {
+  extern __shared__ uint32_t sh_rs[];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int bh = blockIdx.y;
   const int i = blockIdx.x * warps + warp;
@@ -90,15 +95,21 @@ __global__ void rowstats_kernel(SelectParams p, int pow2_t, int warps) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
 
-  float* buf = sh_rows + size_t(warp) * pow2_t;
-  for (int j = lane; j < pow2_t; j += 32) buf[j] = (j < p.n_t) ? S[j] : -INFINITY;
-  __syncwarp();
   float sharp = 0.f;
   const int kk = min(p.k_sparsity, p.n_t);
   if (kk > 0) {
-    bitonic_sort_desc(buf, pow2_t, lane, 32, WarpSync{});
-    if (lane == 0)
-      for (int r = 0; r < kk; ++r) sharp += expf(buf[r] - m) / l;
+    uint32_t* keys = sh_rs + size_t(warp) * stride;
+    uint32_t* hist = sh_rs + size_t(warps) * stride + warp * 256;
+    for (int j = lane; j < p.n_t; j += 32) keys[j] = float_order_key(S[j]);
+    __syncwarp();
+    int n_gt = 0;
+    const uint32_t kth = warp_kth_largest(keys, p.n_t, kk, hist, &n_gt);
+    float acc = 0.f;
+    for (int j = lane; j < p.n_t; j += 32)
+      if (keys[j] > kth) acc += expf(S[j] - m) / l;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    sharp = acc + float(kk - n_gt) * (expf(order_key_to_float(kth) - m) / l);
   }
   if (lane == 0) {
     p.rowmax[size_t(bh) * p.NB + i] = m;
@@ -161,19 +172,30 @@ __global__ void __launch_bounds__(256) outc_kernel(SelectParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// colsum[bh, j] = sum over target rows i < n_t of P[i, n_t + j]; one thread
-// per column, rows added in increasing order.
+// colsum[bh, j] = sum over target rows i < n_t of P[i, n_t + j].  A CTA owns
+// 32 columns; its 8 row groups each add every 8th row in increasing order and
+// the 8 partial sums are combined in a fixed order (deterministic).
 // ---------------------------------------------------------------------------
 __global__ void colsum_kernel(SelectParams p) {
+  __shared__ float part[8][33];
   const int bh = blockIdx.y;
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= p.n_s) return;
-  const float* S = p.scores + size_t(bh) * p.NB * p.NB + p.n_t + j;
+  const int c = threadIdx.x, g = threadIdx.y;
+  const int j = blockIdx.x * 32 + c;
   const float* M = p.rowmax + size_t(bh) * p.NB;
   const float* L = p.rowsum + size_t(bh) * p.NB;
   float acc = 0.f;
-  for (int i = 0; i < p.n_t; ++i) acc += expf(S[size_t(i) * p.NB] - M[i]) / L[i];
-  p.colsum[size_t(bh) * p.n_s + j] = acc;
+  if (j < p.n_s) {
+    const float* S = p.scores + size_t(bh) * p.NB * p.NB + p.n_t + j;
+    for (int i = g; i < p.n_t; i += 8) acc += expf(S[size_t(i) * p.NB] - M[i]) / L[i];
+  }
+  part[g][c] = acc;
+  __syncthreads();
+  if (g == 0 && j < p.n_s) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += part[k][c];
+    p.colsum[size_t(bh) * p.n_s + j] = t;
+  }
 }
 
 }  // namespace
@@ -185,17 +207,18 @@ cudaError_t launch_compressed_attention(const SelectParams& p, cudaStream_t stre
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  const int pow2_t = next_pow2(p.n_t > 0 ? p.n_t : 1);
+  const int stride = p.n_t > 0 ? p.n_t : 1;
   int warps = 8;
-  while (warps > 1 && size_t(warps) * pow2_t * sizeof(float) > 96 * 1024) warps >>= 1;
-  const size_t smem = size_t(warps) * pow2_t * sizeof(float);
+  auto rs_smem = [&](int w) { return size_t(w) * stride * sizeof(uint32_t) + size_t(w) * 256 * sizeof(uint32_t); };
+  while (warps > 1 && rs_smem(warps) > 96 * 1024) warps >>= 1;
+  const size_t smem = rs_smem(warps);
   if (smem > 200 * 1024) return cudaErrorInvalidConfiguration;
   if (smem > 48 * 1024) {
     e = cudaFuncSetAttribute(rowstats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
   }
   dim3 g2((p.NB + warps - 1) / warps, BH);
-  rowstats_kernel<<<g2, warps * 32, smem, stream>>>(p, pow2_t, warps);
+  rowstats_kernel<<<g2, warps * 32, smem, stream>>>(p, warps, stride);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
@@ -205,8 +228,8 @@ cudaError_t launch_compressed_attention(const SelectParams& p, cudaStream_t stre
   if (e != cudaSuccess) return e;
 
   if (p.n_s > 0) {
-    dim3 g4((p.n_s + 127) / 128, BH);
-    colsum_kernel<<<g4, 128, 0, stream>>>(p);
+    dim3 g4((p.n_s + 31) / 32, BH);
+    colsum_kernel<<<g4, dim3(32, 8), 0, stream>>>(p);
     e = cudaGetLastError();
   }
   return e;

@@ -336,6 +336,7 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const STile& t, SSmem<D>& sm, 
   tc::fence_after_sync();
   const float f = ex2((m_ref - m_true) * sl2);
   const float denom = l * f + g_l;
+  const float inv = denom == 0.f ? 0.f : 1.0f / denom;  // the reference's guard: 0 where the denominator is 0
   const int blk = half ? t.blk[1] : t.blk[0];
   const int token = blk * kBlock + (tid & 63);
   const bool write = (half == 0 || t.write1) && token < p.S;
@@ -351,8 +352,7 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const STile& t, SSmem<D>& sm, 
     float o[32];
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
-      const float acc = fmaf(__uint_as_float(ro[e]), f, __uint_as_float(rg[e]));
-      o[e] = denom == 0.f ? 0.f : __fdiv_rn(acc, denom);
+      o[e] = fmaf(__uint_as_float(ro[e]), f, __uint_as_float(rg[e])) * inv;
     }
     if (write) store_out32(p, t.b, token, t.h, oc, c * 32, o, out_row);
   }
