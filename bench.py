@@ -40,7 +40,7 @@ PKG_DIR = os.path.join(REPO, "lightning-unified-video-editor-via-in-context-spar
 sys.path.insert(0, REPO)
 sys.path.insert(0, PKG_DIR)
 
-from in_context_sparse_attention import _capi, editing_sparse_attention, synthetic  # noqa: E402
+from in_context_sparse_attention import _capi, editing_sparse_attention, sharding, synthetic  # noqa: E402
 
 METRIC = "sparse-attn ms/call at 65K joint tokens (40h×128d bf16) 1/2/4/8 GPU; DiT step s"
 WORKLOADS = {"480p": synthetic.WAN480P, "720p": synthetic.WAN720P, "config1": synthetic.CONFIG1}
@@ -256,10 +256,8 @@ def main():
     if args.heads:
         import dataclasses
         w = dataclasses.replace(w, H=args.heads, name=f"{w.name}_h{args.heads}")
-    if w.H % world != 0:
-        raise SystemExit(f"{w.H} heads do not split over {world} GPUs")
-    hp = w.H // world
-    heads = list(range(rank * hp, (rank + 1) * hp))
+    heads = list(sharding.head_range(w.H, rank, world))
+    hp = len(heads)
     q, k, v = synthetic.make_inputs(w, heads=heads, device=dev)
     runner = Runner(q, k, v, w.t_seq_len)
 

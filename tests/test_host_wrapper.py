@@ -1,0 +1,59 @@
+"""The Python drop-in (CPU only): signature, backend validation, dtype rules,
+and that it refuses to run anywhere but on CUDA tensors (no CPU fallback)."""
+import importlib
+import inspect
+
+import pytest
+import torch
+
+import in_context_sparse_attention as ica
+from oracle import icsa_oracle as orc
+
+# the module (the package attribute of the same name is the function)
+esa_mod = importlib.import_module("in_context_sparse_attention.editing_sparse_attention")
+
+
+def test_exports_mirror_the_reference_package():
+    assert set(ica.__all__) == {"Backend", "editing_sparse_attention", "editing_sparse_attention_tilelang"}
+    assert ica.editing_sparse_attention_tilelang is ica.editing_sparse_attention
+
+
+def test_signature_keeps_the_reference_parameters():
+    params = list(inspect.signature(ica.editing_sparse_attention).parameters)
+    assert params[:9] == ["q", "k", "v", "t_seq_len", "s_seq_len", "alpha_2", "alpha_3", "SPARSITY_RATIO", "backend"]
+    sig = inspect.signature(ica.editing_sparse_attention)
+    assert sig.parameters["alpha_2"].default == 1.0
+    assert sig.parameters["SPARSITY_RATIO"].default == 0.0625
+
+
+def test_backend_names():
+    for name in ("b200", "tilelang", "triton"):
+        assert ica.Backend.validate(name) == name
+    with pytest.raises(ValueError, match="Unknown backend"):
+        ica.Backend.validate("flash")
+
+
+def test_cpu_tensors_are_refused():
+    q = torch.randn(1, 128, 2, 64)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        ica.editing_sparse_attention(q, q, q, 64, 64)
+    with pytest.raises(ValueError):
+        ica.editing_sparse_attention(q, q, q, 64, 64, backend="flash")
+
+
+@pytest.mark.parametrize("dts,alpha", [
+    ((torch.bfloat16,) * 3, 1.0),
+    ((torch.float32,) * 3, 1.0),
+    ((torch.float32, torch.float32, torch.bfloat16), torch.zeros(1, 8, 1, 1)),
+    ((torch.bfloat16,) * 3, torch.zeros(1, 8, 1, 1)),
+    ((torch.bfloat16,) * 3, torch.zeros(1, 8, 1, 1, dtype=torch.bfloat16)),
+])
+def test_result_dtypes_follow_torch_promotion(dts, alpha):
+    """Same rules as the reference's `x + out_compress * alpha_2` (with the
+    compressed matmuls in bf16 whenever an input is bf16)."""
+    got = esa_mod._result_dtypes(*dts, alpha)
+    want = orc.result_dtypes(*dts, alpha)
+    assert got == want
+    q = torch.zeros(1, 8, 1, 4, dtype=dts[0])
+    outc = torch.zeros(1, 8, 1, 4, dtype=want[0])
+    assert (q + outc * alpha).dtype == want[2]
