@@ -19,6 +19,8 @@
 // cannot overwrite P(j) before PV(j) has read it.
 #include "icsa_attn_common.cuh"
 
+#include <utility>
+
 namespace icsa {
 
 namespace {
@@ -114,29 +116,37 @@ ICSA_DEV void flat_producer(const AttnParams& p, const AttnMaps& maps, const FTi
   }
 }
 
-template <int D>
-ICSA_DEV void flat_issue_s(FSmem<D>& sm, uint32_t tmem, int tile, int ks) {
+// Descriptors: one base descriptor per operand buffer; each K step adds a
+// compile-time offset to the 14-bit start-address field inside the MMA
+// instruction block (addresses stay below 256 KB, so the field never
+// carries).  The K steps are expanded with a fold expression.
+template <int KK>
+constexpr uint32_t kS_off = uint32_t(((KK >> 2) * kChunkBytes + (KK & 3) * 32) >> 4);
+
+template <int... KK>
+ICSA_DEV void flat_issue_s_seq(uint64_t q_desc, uint64_t k_desc, uint32_t d_tmem, std::integer_sequence<int, KK...>) {
   constexpr uint32_t idesc = tc::make_idesc_bf16(128, 128, false, false);
-  const uint32_t q_addr = smem_u32(sm.q[tile]);
-  const uint32_t k_addr = smem_u32(sm.k[ks]);
-#pragma unroll
-  for (int kk = 0; kk < D / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-    tc::mma_bf16_ss(tmem + tile * 256, tc::make_sw128_desc(q_addr + off, 16, 1024),
-                    tc::make_sw128_desc(k_addr + off, 16, 1024), idesc, kk > 0 ? 1u : 0u);
-  }
+  (tc::mma_bf16_ss_off<kS_off<KK>, kS_off<KK>>(d_tmem, q_desc, k_desc, idesc, KK > 0 ? 1u : 0u), ...);
 }
 
 template <int D>
-ICSA_DEV void flat_issue_pv(FSmem<D>& sm, uint32_t tmem, int tile, int vs, bool accumulate) {
-  constexpr uint32_t idesc = tc::make_idesc_bf16(128, D, false, true);
-  const uint32_t v_addr = smem_u32(sm.v[vs]);
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {  // 128 KV rows, 16 per instruction; P: 8 TMEM columns each
-    tc::mma_bf16_ts(tmem + tile * 256 + 128, tmem + tile * 256 + kk * 8,
-                    tc::make_sw128_desc(v_addr + kk * 16 * 128, kChunkBytes, 1024), idesc,
-                    (accumulate || kk > 0) ? 1u : 0u);
-  }
+ICSA_DEV void flat_issue_s(uint64_t q_desc, uint64_t k_desc, uint32_t d_tmem) {
+  flat_issue_s_seq(q_desc, k_desc, d_tmem, std::make_integer_sequence<int, D / 16>{});
+}
+
+// P.V: 128 KV rows, 16 per instruction; P occupies 8 TMEM columns per step,
+// V advances 16 rows (2048 bytes) per step.
+template <int... KK>
+ICSA_DEV void flat_issue_pv_seq(uint64_t v_desc, uint32_t p_tmem, uint32_t o_tmem, uint32_t acc,
+                                uint32_t idesc, std::integer_sequence<int, KK...>) {
+  (tc::mma_bf16_ts_off<uint32_t(KK * 8), uint32_t((KK * 16 * 128) >> 4)>(o_tmem, p_tmem, v_desc, idesc,
+                                                                         (KK > 0) ? 1u : acc), ...);
+}
+
+template <int D>
+ICSA_DEV void flat_issue_pv(uint64_t v_desc, uint32_t p_tmem, uint32_t o_tmem, bool accumulate) {
+  flat_issue_pv_seq(v_desc, p_tmem, o_tmem, accumulate ? 1u : 0u, tc::make_idesc_bf16(128, D, false, true),
+                    std::make_integer_sequence<int, 8>{});
 }
 
 template <int D>
@@ -144,39 +154,49 @@ ICSA_DEV void flat_mma(const AttnParams& p, const FTile& t, FSmem<D>& sm, uint32
   using C = FCfg<D>;
   volatile int* abort_flag = &sm.abort_flag;
   const int n = t.n_steps;
+  const uint64_t q0 = tc::make_sw128_desc(smem_u32(sm.q[0]), 16, 1024);
+  const uint64_t q1 = tc::make_sw128_desc(smem_u32(sm.q[1]), 16, 1024);
+  const uint64_t k0 = tc::make_sw128_desc(smem_u32(sm.k[0]), 16, 1024);
+  const uint64_t v0 = tc::make_sw128_desc(smem_u32(sm.v[0]), kChunkBytes, 1024);
+  constexpr uint64_t kStageStep = uint64_t(C::kOpBytes >> 4);
+  const uint32_t s0 = tmem, s1 = tmem + 256, o0 = tmem + 128, o1 = tmem + 384;
   if (!mbar_wait(&sm.q_full, 0, p.err, kErrQ, abort_flag)) return;
   if (!mbar_wait(&sm.k_full[0], 0, p.err, kErrKFull, abort_flag)) return;
   tc::fence_after_sync();
-  flat_issue_s<D>(sm, tmem, 0, 0);
+  flat_issue_s<D>(q0, k0, s0);
   tc::mma_commit(&sm.s_full[0]);
-  flat_issue_s<D>(sm, tmem, 1, 0);
+  flat_issue_s<D>(q1, k0, s1);
   tc::mma_commit(&sm.s_full[1]);
   tc::mma_commit(&sm.k_empty[0]);
+  int vs = 0, ks = 1 % C::kKStages;
+  uint32_t vph = 0, kph = (1 / C::kKStages) & 1;
   for (int j = 0; j < n; ++j) {
-    const int vs = j % C::kVStages;
     const bool next = j + 1 < n;
-    const int ks = (j + 1) % C::kKStages;
-    if (!mbar_wait(&sm.v_full[vs], uint32_t(j / C::kVStages) & 1u, p.err, kErrVFull, abort_flag)) return;
+    const uint64_t vd = v0 + uint64_t(vs) * kStageStep;
+    const uint64_t kd = k0 + uint64_t(ks) * kStageStep;
+    if (!mbar_wait(&sm.v_full[vs], vph, p.err, kErrVFull, abort_flag)) return;
     if (!mbar_wait(&sm.p_full[0], uint32_t(j) & 1u, p.err, kErrPFull, abort_flag)) return;
     tc::fence_after_sync();
-    flat_issue_pv<D>(sm, tmem, 0, vs, j > 0);
+    flat_issue_pv<D>(vd, s0, o0, j > 0);
     tc::mma_commit(&sm.o_done[0]);
     if (next) {
-      if (!mbar_wait(&sm.k_full[ks], uint32_t((j + 1) / C::kKStages) & 1u, p.err, kErrKFull, abort_flag)) return;
+      if (!mbar_wait(&sm.k_full[ks], kph, p.err, kErrKFull, abort_flag)) return;
       tc::fence_after_sync();
-      flat_issue_s<D>(sm, tmem, 0, ks);
+      flat_issue_s<D>(q0, kd, s0);
       tc::mma_commit(&sm.s_full[0]);
     }
     if (!mbar_wait(&sm.p_full[1], uint32_t(j) & 1u, p.err, kErrPFull, abort_flag)) return;
     tc::fence_after_sync();
-    flat_issue_pv<D>(sm, tmem, 1, vs, j > 0);
+    flat_issue_pv<D>(vd, s1, o1, j > 0);
     tc::mma_commit(&sm.o_done[1]);
     tc::mma_commit(&sm.v_empty[vs]);
     if (next) {
-      flat_issue_s<D>(sm, tmem, 1, ks);
+      flat_issue_s<D>(q1, kd, s1);
       tc::mma_commit(&sm.s_full[1]);
       tc::mma_commit(&sm.k_empty[ks]);
     }
+    if (++vs == C::kVStages) { vs = 0; vph ^= 1u; }
+    if (++ks == C::kKStages) { ks = 0; kph ^= 1u; }
   }
 }
 

@@ -72,6 +72,33 @@ ICSA_DEV void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uin
       : "memory");
 }
 
+// Same as mma_bf16_ss / mma_bf16_ts with compile-time offsets added to the
+// descriptors (and the A TMEM address) inside the instruction block, so the
+// per-K-step operands are never materialised in registers.
+template <uint32_t AOFF, uint32_t BOFF>
+ICSA_DEV void mma_bf16_ss_off(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 ta, tb;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "add.s64 ta, %1, %5;\n\t"
+      "add.s64 tb, %2, %6;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ta, tb, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(AOFF), "n"(BOFF)
+      : "memory");
+}
+
+template <uint32_t AOFF, uint32_t BOFF>
+ICSA_DEV void mma_bf16_ts_off(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 ta;\n\t.reg .b64 tb;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "add.s32 ta, %1, %5;\n\t"
+      "add.s64 tb, %2, %6;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], tb, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(AOFF), "n"(BOFF)
+      : "memory");
+}
+
 // Arrive (once) on an mbarrier when all previously issued tcgen05.mma of this
 // thread have completed.
 ICSA_DEV void mma_commit(uint64_t* bar) {
