@@ -96,6 +96,19 @@ ICSA_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of a phase (never suspends the thread).
+ICSA_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 ICSA_DEV uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -114,6 +127,26 @@ ICSA_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code, vola
     if (*abort_flag) return false;
     if ((it & 63u) == 63u) {
       uint64_t now = global_timer_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > 1000000000ull) {
+        report_error(err, code);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Same contract as mbar_wait, but polls with the non-suspending test: the
+// caller wakes as soon as the phase completes.  For a single thread whose
+// reaction time is on the critical path (the MMA issuer).
+ICSA_DEV bool mbar_spin_wait(uint64_t* bar, uint32_t parity, int* err, int code, volatile int* abort_flag) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if ((it & 1023u) == 1023u) {
+      const uint64_t now = global_timer_ns();
       if (t0 == 0) t0 = now;
       else if (now - t0 > 1000000000ull) {
         report_error(err, code);

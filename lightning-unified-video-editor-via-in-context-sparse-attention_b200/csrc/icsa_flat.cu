@@ -175,7 +175,7 @@ ICSA_DEV void flat_mma(const AttnParams& p, const FTile& t, FSmem<D>& sm, uint32
     const uint64_t vd = v0 + uint64_t(vs) * kStageStep;
     const uint64_t kd = k0 + uint64_t(ks) * kStageStep;
     if (!mbar_wait(&sm.v_full[vs], vph, p.err, kErrVFull, abort_flag)) return;
-    if (!mbar_wait(&sm.p_full[0], uint32_t(j) & 1u, p.err, kErrPFull, abort_flag)) return;
+    if (!mbar_spin_wait(&sm.p_full[0], uint32_t(j) & 1u, p.err, kErrPFull, abort_flag)) return;
     tc::fence_after_sync();
     flat_issue_pv<D>(vd, s0, o0, j > 0);
     tc::mma_commit(&sm.o_done[0]);
@@ -185,7 +185,7 @@ ICSA_DEV void flat_mma(const AttnParams& p, const FTile& t, FSmem<D>& sm, uint32
       flat_issue_s<D>(q0, kd, s0);
       tc::mma_commit(&sm.s_full[0]);
     }
-    if (!mbar_wait(&sm.p_full[1], uint32_t(j) & 1u, p.err, kErrPFull, abort_flag)) return;
+    if (!mbar_spin_wait(&sm.p_full[1], uint32_t(j) & 1u, p.err, kErrPFull, abort_flag)) return;
     tc::fence_after_sync();
     flat_issue_pv<D>(vd, s1, o1, j > 0);
     tc::mma_commit(&sm.o_done[1]);
