@@ -14,12 +14,13 @@ maximum over ranks: total work per call is fixed, so scaling is "strong".
   sides, max over ranks); the inputs (2 GB) are larger than L2.
 * e2e: the same call through the public Python API with q/k/v copied from
   pinned host memory and the output copied back inside the timed region.
-* roofline: the attention kernel (stage 3, tensor-core bound), algorithmic
-  FLOPs per launch / its CUDA-event duration, against the measured
-  sustained bf16 peak.
+* roofline: the dominant kernel, the dense attention of the flat query
+  blocks (tensor-core bound): algorithmic FLOPs per launch / its CUDA-event
+  duration, against the measured sustained bf16 peak; the block-sparse
+  kernel's figures ride along.
 * cpu_baseline / --impl reference: the CPU restatement of the reference path
   (the reference's PyTorch orchestration + restated kernels) on the host
-  cores, on a bounded sample of the same workload scaled to ms/call.
+  cores: the whole call for one or two heads, scaled to all 40 heads.
 """
 from __future__ import annotations
 
@@ -146,51 +147,64 @@ class Runner:
         _capi.check(lib.icsa_select(pp, a[1], a[2], self.ws.data_ptr(), self.size, st), "icsa_select")
         if ev is not None:
             ev[2].record()
-        _capi.check(lib.icsa_attend(pp, *a, None, self.out.data_ptr(), self.ws.data_ptr(), self.size, st),
-                    "icsa_attend")
+        _capi.check(lib.icsa_attend_dense(pp, *a, None, self.out.data_ptr(), self.ws.data_ptr(), self.size, st),
+                    "icsa_attend_dense")
         if ev is not None:
             ev[3].record()
+        _capi.check(lib.icsa_attend_sparse(pp, *a, None, self.out.data_ptr(), self.ws.data_ptr(), self.size, st),
+                    "icsa_attend_sparse")
+        if ev is not None:
+            ev[4].record()
 
 
 # ---------------------------------------------------------------------------
 # CPU baseline: the oracle port on a bounded sample
 # ---------------------------------------------------------------------------
-def cpu_reference_sample(w, flat_blocks, sparse_blocks, seed_base=0):
-    """Run the CPU restatement for head 0 of workload `w`: pooling, compressed
-    attention, selections and extended KV in full, then `flat_blocks` flat and
-    `sparse_blocks` sparse query blocks.  Returns (scaled ms/call, seconds
-    spent, description)."""
+_CPU_INPUTS = {}
+
+
+def cpu_reference_sample(w, head_count=1, chunk=64, seed_base=0):
+    """Run the CPU restatement of the whole call for the first `head_count`
+    heads of workload `w` (every stage, every query block, in chunks of
+    `chunk` blocks) and scale to all heads.  Returns (ms/call, seconds spent,
+    description)."""
     from oracle import icsa_oracle as orc
     torch.set_num_threads(os.cpu_count() or 1)
-    q, k, v = (x.float() for x in synthetic.make_inputs(w, heads=[0], seed_base=seed_base, device="cpu"))
     t = w.t_seq_len
     c = orc.Counts.make(w.B, w.S, 1, w.D, t)
-    t0 = time.perf_counter()
-    qm, km, vm = orc.block_means(q), orc.block_means(k), orc.block_means(v)
-    s, P, out_c = orc.compressed_attention(*(x.to(torch.bfloat16).permute(0, 2, 1, 3) for x in (qm, km, vm)))
-    sel = orc.select_desc(orc.incontext_keys(P, c.n_t), c.topK)
-    order = orc.select_desc(orc.sharpness_keys(P, c.n_t, c.k_sparsity), c.NB)
-    nk = orc.extended_kv(k, t, sel)[0, 0].to(torch.bfloat16)
-    nv = orc.extended_kv(v, t, sel)[0, 0].to(torch.bfloat16)
-    qb = q[0, :, 0].to(torch.bfloat16).view(c.NB, 64, w.D)
-    kc = orc.block_sums_bf16(nk[None, :, None])[0, 0]
-    vc = orc.block_sums_bf16(nv[None, :, None])[0, 0]
-    t1 = time.perf_counter()
-    fb = order[0, 0, :flat_blocks]
-    qf = qb[fb].reshape(-1, w.D).float()
-    sc = torch.softmax((qf @ nk.float().t()) / (w.D ** 0.5), dim=-1)
-    _ = (sc @ nv.float()).to(torch.bfloat16)
-    t2 = time.perf_counter()
-    sb = order[0, 0, c.num_flat:c.num_flat + sparse_blocks]
-    qsum = orc.block_sums_bf16(qb[sb].reshape(1, -1, 1, w.D))[0, 0]
-    idx = orc.select_desc(qsum.float() @ kc.float().t(), c.top_k)
-    _ = orc.sparse_kernel(qb[sb], nk, nv, kc, vc, idx, c.nkv)
-    t3 = time.perf_counter()
-    per_head = (t1 - t0) + (t2 - t1) * c.num_flat / max(1, flat_blocks) + (t3 - t2) * c.n_sparse / max(1, sparse_blocks)
-    desc = (f"head 0 of {w.H}: pooling, compressed attention, selections and extended KV in full; "
-            f"{flat_blocks}/{c.num_flat} flat and {sparse_blocks}/{c.n_sparse} sparse query blocks; "
-            f"scaled linearly to all blocks and {w.H} heads (fp32 torch on {torch.get_num_threads()} threads)")
-    return per_head * w.H * 1e3, t3 - t0, desc
+    spent = 0.0
+    for h in range(head_count):
+        key = (w.name, h, seed_base)
+        if key not in _CPU_INPUTS:
+            _CPU_INPUTS[key] = tuple(x.float() for x in synthetic.make_inputs(w, heads=[h], seed_base=seed_base,
+                                                                              device="cpu"))
+        q, k, v = _CPU_INPUTS[key]
+        t0 = time.perf_counter()
+        qm, km, vm = orc.block_means(q), orc.block_means(k), orc.block_means(v)
+        s, P, out_c = orc.compressed_attention(*(x.to(torch.bfloat16).permute(0, 2, 1, 3) for x in (qm, km, vm)))
+        sel = orc.select_desc(orc.incontext_keys(P, c.n_t), c.topK)
+        order = orc.select_desc(orc.sharpness_keys(P, c.n_t, c.k_sparsity), c.NB)
+        nk = orc.extended_kv(k, t, sel)[0, 0].to(torch.bfloat16)
+        nv = orc.extended_kv(v, t, sel)[0, 0].to(torch.bfloat16)
+        qb = q[0, :, 0].to(torch.bfloat16).view(c.NB, 64, w.D)
+        kc = orc.block_sums_bf16(nk[None, :, None])[0, 0]
+        vc = orc.block_sums_bf16(nv[None, :, None])[0, 0]
+        nkf, nvf = nk.float(), nv.float()
+        for i in range(0, c.num_flat, chunk):
+            fb = order[0, 0, i:min(c.num_flat, i + chunk)]
+            qf = qb[fb].reshape(-1, w.D).float()
+            sc = torch.softmax((qf @ nkf.t()) / (w.D ** 0.5), dim=-1)
+            _ = (sc @ nvf).to(torch.bfloat16)
+        for i in range(c.num_flat, c.NB, chunk):
+            sb = order[0, 0, i:min(c.NB, i + chunk)]
+            qsum = orc.block_sums_bf16(qb[sb].reshape(1, -1, 1, w.D))[0, 0]
+            idx = orc.select_desc(qsum.float() @ kc.float().t(), c.top_k)
+            _ = orc.sparse_kernel(qb[sb], nk, nv, kc, vc, idx, c.nkv)
+        spent += time.perf_counter() - t0
+    desc = (f"the whole call for {head_count} of {w.H} heads (pooling, compressed attention, selections, "
+            f"extended KV, all {c.num_flat} flat and {c.n_sparse} sparse query blocks), scaled to {w.H} heads; "
+            f"fp32 torch on {torch.get_num_threads()} threads")
+    return spent / head_count * w.H * 1e3, spent, desc
 
 
 def run_reference_arm(args, rank):
@@ -199,12 +213,11 @@ def run_reference_arm(args, rank):
     if rank != 0:
         return
     w = WORKLOADS[args.workload]
-    fb = sb = 4
     for _ in range(args.warmup):
-        cpu_reference_sample(w, fb, sb)
+        cpu_reference_sample(w)
     vals = []
     for _ in range(args.steps):
-        ms, _, desc = cpu_reference_sample(w, fb, sb)
+        ms, _, desc = cpu_reference_sample(w)
         vals.append(ms)
     value = statistics.mean(vals)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "ms/call", "n_gpus": args.gpus,
@@ -233,6 +246,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-heads", type=int, default=2, help="heads the CPU baseline runs in full")
     ap.add_argument("--heads", type=int, default=0, help="run only this many heads (profiling of a small case)")
     args = ap.parse_args()
 
@@ -269,7 +283,7 @@ def main():
     for _ in range(args.warmup):
         runner.step()
     barrier()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
     clocks = ClockSampler(dev)
     clocks.start()
     barrier()
@@ -283,7 +297,7 @@ def main():
     clk = clocks.stop()
     elapsed = t_start.elapsed_time(t_end)
     stage = {n: statistics.mean(e[i].elapsed_time(e[i + 1]) for e in evs) for i, n in
-             enumerate(("pool", "select", "attend"))}
+             enumerate(("pool", "select", "attend_dense", "attend_sparse"))}
     rc = runner.lib.icsa_device_status(runner.ws.data_ptr(), torch.cuda.current_stream().cuda_stream)
     _capi.check(rc, "icsa_device_status")
 
@@ -310,23 +324,27 @@ def main():
                "d2h_bytes_per_step": q.numel() * q.element_size()}
 
     ms = elapsed / args.steps
-    att = stage["attend"]
     if dist is not None:
-        t = torch.tensor([ms, att, e2e["value"] if e2e else 0.0], device=dev)
+        names = sorted(stage)
+        t = torch.tensor([ms, e2e["value"] if e2e else 0.0] + [stage[n] for n in names], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, att = float(t[0]), float(t[1])
+        ms = float(t[0])
         if e2e:
-            e2e["value"] = float(t[2])
+            e2e["value"] = float(t[1])
+        stage = {n: float(x) for n, x in zip(names, t[2:])}
     sustained, burst, hbm, src = peaks()
-    flops, _, _ = attention_flops(runner.p, runner.L.n_sparse)
-    achieved = flops / (att * 1e-3) / 1e12
+    _, flops, sparse_flops = attention_flops(runner.p, runner.L.n_sparse)
+    # dominant kernel: the dense attention of the flat query blocks (one launch per call)
+    achieved = flops / (stage["attend_dense"] * 1e-3) / 1e12
+    sparse_achieved = sparse_flops / (stage["attend_sparse"] * 1e-3) / 1e12
     traffic = None
-    tpath = os.path.join(REPO, "profiles", "attention_traffic.json")
+    tpath = os.path.join(REPO, "profiles", "flat_kernel_traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
             tr = json.load(f)
-        if tr.get("workload") == w.name and tr.get("heads") == hp:
-            traffic = tr.get("dram_bytes_per_launch")
+        # measured on a smaller head count; DRAM bytes grow in proportion to the heads
+        if tr.get("workload") == w.name.split("_h")[0] and tr.get("heads"):
+            traffic = tr["dram_bytes_per_launch"] * hp / tr["heads"]
 
     if rank == 0:
         line = {"metric": METRIC, "value": ms, "unit": "ms/call", "n_gpus": world, "steps": args.steps,
@@ -334,15 +352,17 @@ def main():
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded blurred-field generator)",
                 "config": config_dict(w, world),
                 "stages_ms": stage,
-                "roofline": {"bound": "tensor", "kernel": "attn_kernel (stage 3)", "achieved": achieved,
-                             "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained,
+                "roofline": {"bound": "tensor", "kernel": "flat_kernel (dense attention of the flat blocks)",
+                             "achieved": achieved, "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained,
                              "peak_kind": f"{src} sustained bf16", "frac_of_burst": achieved / burst,
-                             "traffic": traffic, "flops_per_launch": flops},
+                             "traffic": traffic, "flops_per_launch": flops,
+                             "sparse_kernel": {"achieved": sparse_achieved, "frac": sparse_achieved / sustained,
+                                               "flops_per_launch": sparse_flops}},
                 "clocks": clk, "gpu_launches": KERNELS_PER_CALL_ALIGNED * args.steps}
         if e2e:
             line["e2e"] = e2e
         if world == 1 and not args.no_cpu_baseline:
-            cms, secs, desc = cpu_reference_sample(w, 64, 64)
+            cms, secs, desc = cpu_reference_sample(w, head_count=args.cpu_heads)
             line["cpu_baseline"] = {"value": cms, "unit": "ms/call", "cores": torch.get_num_threads(),
                                     "kind": "port", "sample": desc, "sample_seconds": secs}
         print(json.dumps(line), flush=True)

@@ -170,6 +170,19 @@ ICSA_API int icsa_attend(const icsa_problem* p, const void* q, const void* k, co
                 void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
+ * The two halves of stage 3, for per-kernel timing: icsa_attend_dense runs
+ * the dense attention of the flat query blocks (the flash_attn_func call,
+ * editing_sparse_attention.py:211-215, with its scatter and residual,
+ * :217-232); icsa_attend_sparse the block-sparse attention of the remaining
+ * blocks (tilelang_kernels.py:681-997 with the same epilogue).  Each writes
+ * only its own query blocks of `out`; together they equal icsa_attend.
+ */
+ICSA_API int icsa_attend_dense(const icsa_problem* p, const void* q, const void* k, const void* v, const void* alpha,
+                               void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+ICSA_API int icsa_attend_sparse(const icsa_problem* p, const void* q, const void* k, const void* v, const void* alpha,
+                                void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
  * Synchronises `stream` and returns ICSA_OK or the status a device-side
  * bounded wait recorded in the workspace during the preceding calls.
  */

@@ -251,8 +251,11 @@ int run_select(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, 
   return ICSA_OK;
 }
 
+constexpr int kAttendDense = 1, kAttendSparse = 2;
+
 int run_attend(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, const void* q, const void* k,
-               const void* v, const void* alpha, void* out, cudaStream_t stream) {
+               const void* v, const void* alpha, void* out, cudaStream_t stream,
+               int parts = kAttendDense | kAttendSparse) {
   if (out == nullptr) return fail(ICSA_ERR_INVALID, "output pointer is NULL");
   if (p->alpha_mode == ICSA_ALPHA_TENSOR && alpha == nullptr) return fail(ICSA_ERR_INVALID, "alpha tensor is NULL");
   const bool aligned = (p->t_seq_len % icsa::kBlock) == 0;
@@ -285,10 +288,15 @@ int run_attend(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, 
   for (int i = 0; i < 4; ++i) a.alpha_strides[i] = p->alpha_strides[i];
   a.out = out; a.out_dtype = p->out_dtype;
   a.err = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + L.err);
-  cudaError_t e = icsa::launch_flat_attention(a, maps, p->D, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "dense attention");
-  e = icsa::launch_sparse_attention(a, maps, p->D, stream);
-  return e == cudaSuccess ? ICSA_OK : cuda_fail(e, "sparse attention");
+  if (parts & kAttendDense) {
+    cudaError_t e = icsa::launch_flat_attention(a, maps, p->D, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "dense attention");
+  }
+  if (parts & kAttendSparse) {
+    cudaError_t e = icsa::launch_sparse_attention(a, maps, p->D, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "sparse attention");
+  }
+  return ICSA_OK;
 }
 
 }  // namespace
@@ -373,6 +381,24 @@ int icsa_attend(const icsa_problem* p, const void* q, const void* k, const void*
   if (rc != ICSA_OK) return rc;
   if (q == nullptr || k == nullptr || v == nullptr) return fail(ICSA_ERR_INVALID, "q, k and v must be non-NULL");
   return run_attend(p, L, workspace, q, k, v, alpha, out, stream);
+}
+
+int icsa_attend_dense(const icsa_problem* p, const void* q, const void* k, const void* v, const void* alpha,
+                      void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  icsa_workspace_layout L;
+  int rc = check_call(p, workspace, workspace_bytes, &L);
+  if (rc != ICSA_OK) return rc;
+  if (q == nullptr || k == nullptr || v == nullptr) return fail(ICSA_ERR_INVALID, "q, k and v must be non-NULL");
+  return run_attend(p, L, workspace, q, k, v, alpha, out, stream, kAttendDense);
+}
+
+int icsa_attend_sparse(const icsa_problem* p, const void* q, const void* k, const void* v, const void* alpha,
+                       void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  icsa_workspace_layout L;
+  int rc = check_call(p, workspace, workspace_bytes, &L);
+  if (rc != ICSA_OK) return rc;
+  if (q == nullptr || k == nullptr || v == nullptr) return fail(ICSA_ERR_INVALID, "q, k and v must be non-NULL");
+  return run_attend(p, L, workspace, q, k, v, alpha, out, stream, kAttendSparse);
 }
 
 int icsa_forward(const icsa_problem* p, const void* q, const void* k, const void* v, const void* alpha, void* out,

@@ -1,7 +1,7 @@
 // Shared definitions for the in-context sparse attention kernels (sm_100a).
 //
 // Everything here is plain CUDA C++ plus inline PTX for the Blackwell
-// asynchronous machinery: mbarriers, TMA tensor loads (no multicast anywhere),
+// asynchronous machinery: mbarriers, TMA tensor loads (each CTA loads for itself),
 // and the tcgen05 tensor-memory / MMA instructions.
 #pragma once
 
@@ -158,7 +158,7 @@ ICSA_DEV bool mbar_spin_wait(uint64_t* bar, uint32_t parity, int* err, int code,
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tensor) loads.  Single-CTA form only: no .multicast::cluster.
+// TMA (tensor) loads.  Single-CTA form only: each load lands in the issuing CTA.
 // ---------------------------------------------------------------------------
 ICSA_DEV void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
   asm volatile(

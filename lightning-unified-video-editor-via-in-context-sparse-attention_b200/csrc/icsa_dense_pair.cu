@@ -1,0 +1,435 @@
+// Dense attention for the "flat" query blocks (the reference's
+// flash_attn_func call, editing_sparse_attention.py:211-215, fused with the
+// scatter and residual of :217-232), D = 128, on SM pairs.
+//
+// A cluster of two CTAs computes a 256-row query tile (four 64-token flat
+// blocks): the leader issues M = 256 tcgen05 MMAs (cta_group::2), each CTA
+// holds its own 128 query rows, half of every 128-row key tile (64 keys x
+// 128 d) and half of every value tile (128 keys x 64 d).  Per CTA this reads
+// 64 KB of operands from shared memory per 128 keys (plus 32 KB of TMA
+// writes), under the 128 B/clk the tensor core can draw from it.
+//
+// TMEM (512 columns per CTA):
+//   S(j) in buffer j%2 at [0,128) / [128,256)   fp32 scores, lane = query row
+//   P(j) in buffer j%2 at [256,320) / [320,384) bf16 pairs (A operand of P.V)
+//   O at [384,512)                               fp32 accumulator
+// Because P has its own columns, S(j+2) may overwrite S buffer j%2 as soon as
+// the softmax has copied S(j) to registers; the softmax never waits for its
+// own P.V, and the tensor core works from a queue filled two steps ahead:
+//   S(0) S(1) | S(j+2) after softmax(j) read S(j), P.V(j) after P(j) | ...
+//
+// Roles per CTA (384 threads):
+//   warps 0-3 / 4-7  softmax of key columns [0,64) / [64,128) of every row
+//                    (thread <-> TMEM lane <-> query row); the two halves of
+//                    a row exchange their maxima through shared memory;
+//   warp 8           TMA producer (Q once, then the K and V rings);
+//   warp 9           TMEM allocation; in the leader, the MMA issuer.
+#include "icsa_attn_common.cuh"
+#include "icsa_pair.cuh"
+
+#include <utility>
+
+namespace icsa {
+
+namespace {
+
+using namespace attn;
+
+constexpr int kPThreads = 384;
+constexpr int kPProducerWarp = 8;
+constexpr int kPMmaWarp = 9;
+constexpr int kPStages = 4;
+constexpr int kPQBytes = 128 * 128 * 2;  // this CTA's 128 query rows, two 64-wide d chunks of 16 KB
+constexpr int kPKBytes = 64 * 128 * 2;   // 64 key rows x 128 d, two d chunks of 8 KB
+constexpr int kPVBytes = 128 * 64 * 2;   // 128 value rows x this CTA's 64 d
+constexpr uint32_t kTmS = 0, kTmP = 256, kTmO = 384, kPTmemCols = 512;
+
+struct __align__(1024) PSmem {
+  uint8_t q[kPQBytes];
+  uint8_t k[kPStages][kPKBytes];
+  uint8_t v[kPStages][kPVBytes];
+  float mref[2][128];  // [warpgroup][row] m_ref after that warpgroup's latest step
+  float lsum[2][128];  // epilogue: partial row sums and their origins
+  float lmax[2][128];
+  uint64_t q_full;
+  uint64_t k_full[kPStages], k_empty[kPStages];
+  uint64_t v_full[kPStages], v_empty[kPStages];
+  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  uint64_t mma_fin;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+static_assert(sizeof(PSmem) + 1024 <= 232448, "pair kernel shared memory exceeds 227 KB");
+
+struct PTile {
+  int bh, b, h;
+  int blk[2];    // query blocks of rows [0,64) and [64,128) of this CTA
+  int write[2];  // 0 for a duplicate filling an incomplete group
+  int n_steps;   // key steps of 128 rows
+  uint32_t rank;
+};
+
+ICSA_DEV PTile decode_pair_tile(const AttnParams& p) {
+  PTile t;
+  t.rank = pair::cluster_rank();
+  const int pr = blockIdx.x >> 1;
+  const int groups = (p.num_flat + 3) / 4;
+  t.bh = pr / groups;
+  const int g = pr % groups;
+  t.b = t.bh / p.H;
+  t.h = t.bh % p.H;
+  const int* order = p.order + size_t(t.bh) * p.NB;  // flat blocks come first
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = 4 * g + 2 * int(t.rank) + i;
+    t.write[i] = r < p.num_flat;
+    t.blk[i] = order[t.write[i] ? r : p.num_flat - 1];
+  }
+  t.n_steps = (p.nkv + 1) / 2;
+  return t;
+}
+
+ICSA_DEV void pair_producer(const AttnParams& p, const AttnMaps& maps, const PTile& t, PSmem& sm) {
+  volatile int* abort_flag = &sm.abort_flag;
+  const bool leader = t.rank == 0;
+  if (leader) mbar_arrive_expect_tx(&sm.q_full, 2 * kPQBytes);
+  const uint32_t q_full = pair::mapa(&sm.q_full, 0);
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+      pair::tma_load_4d(sm.q + c * kChunkBytes + half * (kChunkBytes / 2), &maps.q, q_full, c * 64, t.h,
+                        t.blk[half] * kBlock, t.b);
+  const int* rows = p.kv_rows + size_t(t.bh) * p.nkv;
+  for (int j = 0; j < t.n_steps; ++j) {
+    const int s = j % kPStages;
+    const uint32_t ph = uint32_t(j / kPStages) & 1u;
+    const int r0 = rows[2 * j];
+    const int r1 = (2 * j + 1 < p.nkv) ? rows[2 * j + 1] : r0;  // missing half: masked by the softmax
+    // keys: this CTA's 64 of the 128 (N split)
+    if (!mbar_wait(&sm.k_empty[s], ph ^ 1u, p.err, kErrKEmpty, abort_flag)) return;
+    if (leader) mbar_arrive_expect_tx(&sm.k_full[s], 2 * kPKBytes);
+    const uint32_t k_full = pair::mapa(&sm.k_full[s], 0);
+    const int rk = t.rank ? r1 : r0;
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+      pair::tma_load_4d(sm.k[s] + c * (kPKBytes / 2), &maps.k, k_full, c * 64, t.h, rk, t.b);
+    // values: all 128 keys, this CTA's 64 of the 128 d (N split)
+    if (!mbar_wait(&sm.v_empty[s], ph ^ 1u, p.err, kErrVEmpty, abort_flag)) return;
+    if (leader) mbar_arrive_expect_tx(&sm.v_full[s], 2 * kPVBytes);
+    const uint32_t v_full = pair::mapa(&sm.v_full[s], 0);
+    pair::tma_load_4d(sm.v[s], &maps.v, v_full, int(t.rank) * 64, t.h, r0, t.b);
+    pair::tma_load_4d(sm.v[s] + kPVBytes / 2, &maps.v, v_full, int(t.rank) * 64, t.h, r1, t.b);
+  }
+}
+
+// S = Q K^T over d = 128: eight K = 16 steps; Q chunks are 16 KB apart, key
+// chunks 8 KB apart; 32 bytes per step inside a 128-byte swizzled row.
+template <int KK>
+constexpr uint32_t kQOff = uint32_t(((KK >> 2) * kChunkBytes + (KK & 3) * 32) >> 4);
+template <int KK>
+constexpr uint32_t kKOff = uint32_t(((KK >> 2) * (kPKBytes / 2) + (KK & 3) * 32) >> 4);
+
+template <int... KK>
+ICSA_DEV void pair_issue_s_seq(uint64_t q_desc, uint64_t k_desc, uint32_t d_tmem, std::integer_sequence<int, KK...>) {
+  constexpr uint32_t idesc = tc::make_idesc_bf16(256, 128, false, false);
+  (pair::mma_ss_elect<kQOff<KK>, kKOff<KK>>(d_tmem, q_desc, k_desc, idesc, KK > 0 ? 1u : 0u), ...);
+}
+
+// O += P V over 128 keys: eight K = 16 steps; P advances 8 TMEM columns, V
+// (MN-major, 128-byte rows of 64 d) advances 16 rows = 2048 bytes.
+template <int... KK>
+ICSA_DEV void pair_issue_pv_seq(uint64_t v_desc, uint32_t p_tmem, uint32_t o_tmem, uint32_t acc,
+                                std::integer_sequence<int, KK...>) {
+  constexpr uint32_t idesc = tc::make_idesc_bf16(256, 128, false, true);
+  (pair::mma_ts_elect<uint32_t(KK * 8), uint32_t((KK * 16 * 128) >> 4)>(o_tmem, p_tmem, v_desc, idesc,
+                                                                         (KK > 0) ? 1u : acc),
+   ...);
+}
+
+// MMA issuer: all 32 lanes of warp 9 of the leader run this loop (waits are
+// warp-uniform, one elected lane issues each instruction).
+ICSA_DEV void pair_mma(const AttnParams& p, const PTile& t, PSmem& sm, uint32_t tmem) {
+  volatile int* abort_flag = &sm.abort_flag;
+  const int n = t.n_steps;
+  const uint64_t qd = tc::make_sw128_desc(smem_u32(sm.q), 16, 1024);
+  const uint64_t kd0 = tc::make_sw128_desc(smem_u32(sm.k[0]), 16, 1024);
+  const uint64_t vd0 = tc::make_sw128_desc(smem_u32(sm.v[0]), kPVBytes, 1024);
+  constexpr uint64_t kKStep = uint64_t(kPKBytes >> 4), kVStep = uint64_t(kPVBytes >> 4);
+  if (!warp_mbar_wait(&sm.q_full, 0, p.err, kErrQ, abort_flag)) return;
+
+  auto issue_s = [&](int j) -> bool {
+    const int s = j % kPStages;
+    if (!warp_mbar_wait(&sm.k_full[s], uint32_t(j / kPStages) & 1u, p.err, kErrKFull, abort_flag)) return false;
+    tc::fence_after_sync();
+    pair_issue_s_seq(qd, kd0 + uint64_t(s) * kKStep, tmem + kTmS + 128u * uint32_t(j & 1),
+                     std::make_integer_sequence<int, 8>{});
+    pair::commit_both_elect(&sm.s_full[j & 1]);
+    pair::commit_both_elect(&sm.k_empty[s]);
+    return true;
+  };
+
+  auto issue_pv = [&](int j) -> bool {
+    const int b = j & 1, s = j % kPStages;
+    if (!warp_mbar_wait(&sm.p_full[b], uint32_t(j >> 1) & 1u, p.err, kErrPFull, abort_flag)) return false;
+    if (!warp_mbar_wait(&sm.v_full[s], uint32_t(j / kPStages) & 1u, p.err, kErrVFull, abort_flag)) return false;
+    tc::fence_after_sync();
+    pair_issue_pv_seq(vd0 + uint64_t(s) * kVStep, tmem + kTmP + 64u * uint32_t(b), tmem + kTmO, j > 0 ? 1u : 0u,
+                      std::make_integer_sequence<int, 8>{});
+    pair::commit_both_elect(&sm.pv_done[b]);
+    pair::commit_both_elect(&sm.v_empty[s]);
+    return true;
+  };
+
+  // S(j+2) is issued as soon as both CTAs' softmax has read S(j) (buffer j%2),
+  // P.V(j) once P(j) is written.  (Deferring P.V(j) behind S(j+3) measured
+  // slower: it delays the P buffer release.)
+  if (!issue_s(0)) return;
+  if (n > 1 && !issue_s(1)) return;
+  for (int j = 0; j < n; ++j) {
+    if (j + 2 < n) {
+      if (!warp_mbar_wait(&sm.s_free[j & 1], uint32_t(j >> 1) & 1u, p.err, kErrSEmpty, abort_flag)) return;
+      if (!issue_s(j + 2)) return;
+    }
+    if (!issue_pv(j)) return;
+  }
+}
+
+// Softmax: warpgroup w handles the key steps j with j % 2 == w, over all 128
+// keys of the step (thread <-> TMEM lane <-> query row).  The running maximum
+// (the exponent origin m_ref of O) passes from one warpgroup to the other
+// every step through shared memory: the producer of step j publishes m_ref(j)
+// with a non-blocking named-barrier arrive and the consumer of step j+1
+// waits on the same barrier, so the two warpgroups run half a step apart and
+// one's loads and stores overlap the other's exponentials.
+// Each warpgroup keeps its own partial row sum l_w relative to the m_ref of
+// its last step; the epilogue brings both to the final origin.
+// Neither warpgroup may leave the loop early (the named barriers pair them):
+// after a failed wait the abort flag is set, every later wait returns at
+// once, the loop runs on over stale data, and the error code marks the
+// result invalid.
+ICSA_DEV void pair_softmax(const AttnParams& p, const PTile& t, PSmem& sm, uint32_t tmem) {
+  volatile int* abort_flag = &sm.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w = warp >> 2;                 // this warpgroup's step parity
+  const int row = threadIdx.x & 127;       // query row = TMEM lane
+  // named barriers 1-4: m_ref from warpgroup 0 to 1; 5-8: from 1 to 0 (per 32 rows)
+  const uint32_t bar_to_other = 1u + 4u * uint32_t(w) + uint32_t(warp & 3);
+  const uint32_t bar_from_other = 1u + 4u * uint32_t(w ^ 1) + uint32_t(warp & 3);
+  const uint32_t lanes = uint32_t((warp & 3) * 32) << 16;
+  const uint32_t s_base = tmem + lanes + kTmS + 128u * uint32_t(w);
+  const uint32_t p_base = tmem + lanes + kTmP + 64u * uint32_t(w);
+  const uint32_t o_base = tmem + lanes + kTmO;
+  const uint32_t s_free = pair::mapa(&sm.s_free[w], 0);
+  const uint32_t p_full = pair::mapa(&sm.p_full[w], 0);
+  const float sl2 = p.scale_log2;
+  const int n = t.n_steps;
+  float m_w = -INFINITY, l_w = 0.f;  // partial row sum and its exponent origin
+
+  for (int j = w; j < n; j += 2) {
+    const uint32_t par = uint32_t(j >> 1) & 1u;
+    warp_mbar_wait(&sm.s_full[w], par, p.err, kErrSFull, abort_flag);
+    tc::fence_after_sync();
+    float s[128];
+    tmem_load_row128(s_base, s);
+    // S buffer w may now be overwritten by S(j+2)
+    tc::fence_before_sync();
+    __syncwarp();
+    if (lane == 0) pair::arrive_cluster_relaxed(s_free);
+    __syncwarp();
+
+    const int hi = p.tkv - j * 128;  // extended-KV rows beyond tkv are not keys
+    if (hi < 128) {
+#pragma unroll
+      for (int c = 0; c < 128; ++c)
+        if (c >= hi) s[c] = -INFINITY;
+    }
+    const float mx = max128(s);
+    float m_prev = -INFINITY;
+    if (j > 0) {
+      pair::named_sync(bar_from_other, 64);
+      m_prev = sm.mref[w ^ 1][row];
+    }
+    const bool need = (mx - m_prev) * sl2 > kRescaleThreshold;
+    const float m_ref = need ? mx : m_prev;
+    if (j + 1 < n) {
+      sm.mref[w][row] = m_ref;
+      pair::named_arrive(bar_to_other, 64);
+    }
+    if (m_w != m_ref) {
+      l_w = (m_w == -INFINITY) ? 0.f : l_w * ex2((m_w - m_ref) * sl2);
+      m_w = m_ref;
+    }
+    // P buffer w was last read by P.V(j-2)
+    if (j >= 2) warp_mbar_wait(&sm.pv_done[w], uint32_t((j - 2) >> 1) & 1u, p.err, kErrPvDone, abort_flag);
+    tc::fence_after_sync();
+    const float neg = -m_ref * sl2;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+    for (int c = 0; c < 128; c += 4) {
+      ffma2(s[c], s[c + 1], s[c], s[c + 1], sl2, sl2, neg, neg);
+      ffma2(s[c + 2], s[c + 3], s[c + 2], s[c + 3], sl2, sl2, neg, neg);
+      s[c] = ex2(s[c]);
+      s[c + 1] = ex2(s[c + 1]);
+      s[c + 2] = ex2(s[c + 2]);
+      s[c + 3] = ex2(s[c + 3]);
+      fadd2(a0, a1, a0, a1, s[c], s[c + 1]);
+      fadd2(a2, a3, a2, a3, s[c + 2], s[c + 3]);
+      if ((c & 63) == 60) {
+        // 64 probabilities done: pack them and write them to the P buffer
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pk[e] = pack_bf16x2(s[(c & ~63) + 2 * e], s[(c & ~63) + 2 * e + 1]);
+        tc::tmem_st32(p_base + uint32_t(c >> 6) * 32u, pk);
+      }
+    }
+    l_w += (a0 + a1) + (a2 + a3);
+    if (j > 0 && __any_sync(0xffffffffu, need)) {
+      // O holds P.V up to step j-1 relative to m_prev: rescale it to m_ref
+      warp_mbar_wait(&sm.pv_done[w ^ 1], uint32_t((j - 1) >> 1) & 1u, p.err, kErrPvDone, abort_flag);
+      tc::fence_after_sync();
+      const float alpha = need ? ex2((m_prev - m_ref) * sl2) : 1.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tc::tmem_ld32(o_base + 32u * uint32_t(c), r);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+        tc::tmem_st32(o_base + 32u * uint32_t(c), r);
+      }
+    }
+    tc::tmem_wait_st();
+    tc::fence_before_sync();
+    __syncwarp();
+    if (lane == 0) pair::arrive_cluster_relaxed(p_full);
+    __syncwarp();
+  }
+
+  // epilogue: both partial sums to the final origin; this warpgroup writes
+  // features [64w, 64w + 64) of its row
+  const int last = n - 1;
+  warp_mbar_wait(&sm.pv_done[last & 1], uint32_t(last >> 1) & 1u, p.err, kErrPvDone, abort_flag);
+  tc::fence_after_sync();
+  sm.lsum[w][row] = l_w;
+  sm.lmax[w][row] = m_w;
+  pair::named_sync(9u + uint32_t(warp & 3), 64);
+  const float m_fin = sm.lmax[last & 1][row];  // m_ref of the last step
+  float lt = 0.f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float mi = sm.lmax[i][row], li = sm.lsum[i][row];
+    if (mi != -INFINITY) lt += (mi == m_fin) ? li : li * ex2((mi - m_fin) * sl2);
+  }
+  const float inv = lt == 0.f ? 0.f : 1.0f / lt;
+  const int blk = (row < 64) ? t.blk[0] : t.blk[1];
+  const int wr = (row < 64) ? t.write[0] : t.write[1];
+  const int token = blk * kBlock + (row & 63);
+  const bool write = wr && token < p.S;
+  const float* oc = p.outc + (size_t(t.bh) * p.NB + blk) * 128;
+  const size_t out_row = ((size_t(t.b) * p.S + token) * p.H + t.h) * 128;
+#pragma unroll 1
+  for (int c = 0; c < 2; ++c) {
+    uint32_t r[32];
+    __syncwarp();
+    tc::tmem_ld32(o_base + 64u * uint32_t(w) + 32u * uint32_t(c), r);
+    tc::tmem_wait_ld();
+    float o[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(r[e]) * inv;
+    if (write) store_out32(p, t.b, token, t.h, oc, 64 * w + 32 * c, o, out_row);
+  }
+}
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
+    dense_pair_kernel(const AttnParams p, const __grid_constant__ AttnMaps maps) {
+  extern __shared__ uint8_t smem_raw[];
+  PSmem& sm = *reinterpret_cast<PSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const PTile t = decode_pair_tile(p);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int i = 0; i < kPStages; ++i) {
+      mbar_init(&sm.k_full[i], 1);
+      mbar_init(&sm.k_empty[i], 1);
+      mbar_init(&sm.v_full[i], 1);
+      mbar_init(&sm.v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.s_full[i], 1);
+      mbar_init(&sm.pv_done[i], 1);
+      mbar_init(&sm.s_free[i], 8);  // one arrival per warp of the step's warpgroup, both CTAs
+      mbar_init(&sm.p_full[i], 8);
+    }
+    mbar_init(&sm.mma_fin, 1);
+    sm.abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == kPMmaWarp) {
+    pair::tmem_alloc(&sm.tmem_base, kPTmemCols);
+    pair::tmem_relinquish();
+  }
+  if (warp == kPProducerWarp && lane == 0) {
+    prefetch_tensormap(&maps.q);
+    prefetch_tensormap(&maps.k);
+    prefetch_tensormap(&maps.v);
+  }
+  tc::fence_before_sync();
+  pair::cluster_sync();
+  tc::fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+
+  // Register split: 384 threads launch with 168 registers each; warpgroup 2
+  // (producer, MMA issuer, two idle warps) gives registers back so that the
+  // softmax warpgroups can hold a whole 128-column row:
+  // 256 x 216 + 128 x 72 = 384 x 168.  setmaxnreg is executed by every warp of
+  // a warpgroup.
+  if (warp < 8) {
+    tc::reg_alloc<216>();
+    pair_softmax(p, t, sm, tmem);
+  } else {
+    tc::reg_dealloc<72>();
+  }
+  if (warp == kPProducerWarp) {
+    if (lane == 0) {
+      pair_producer(p, maps, t, sm);
+      if (sm.abort_flag && t.rank == 0) {
+        // the leader's full barriers count the bytes of both CTAs: let every
+        // copy still in flight land before either CTA releases its memory
+        for (int j = max(0, t.n_steps - kPStages); j < t.n_steps; ++j) {
+          drain_wait(&sm.k_full[j % kPStages], uint32_t(j / kPStages) & 1u, p.err);
+          drain_wait(&sm.v_full[j % kPStages], uint32_t(j / kPStages) & 1u, p.err);
+        }
+        drain_wait(&sm.q_full, 0, p.err);
+      }
+    }
+  } else if (warp == kPMmaWarp) {
+    if (t.rank == 0) {
+      pair_mma(p, t, sm, tmem);
+      pair::commit_both_elect(&sm.mma_fin);
+      if (lane == 0) drain_wait(&sm.mma_fin, 0, p.err);
+    }
+  }
+  __syncwarp();
+  tc::fence_before_sync();
+  pair::cluster_sync();
+  if (warp == kPMmaWarp) {
+    tc::fence_after_sync();
+    pair::tmem_dealloc(tmem, kPTmemCols);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_dense_pair_attention(const AttnParams& p, const AttnMaps& maps, cudaStream_t stream) {
+  const int pairs = p.B * p.H * ((p.num_flat + 3) / 4);
+  if (pairs == 0) return cudaSuccess;
+  const size_t smem = sizeof(PSmem) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(dense_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  dense_pair_kernel<<<2 * pairs, kPThreads, smem, stream>>>(p, maps);
+  return cudaGetLastError();
+}
+
+}  // namespace icsa

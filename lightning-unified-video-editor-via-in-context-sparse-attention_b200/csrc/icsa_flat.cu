@@ -379,6 +379,7 @@ __global__ void __launch_bounds__(kFThreads, 1) flat_kernel(const AttnParams p, 
 cudaError_t launch_flat_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream) {
   const int ctas = p.B * p.H * ((p.num_flat + 3) / 4);
   if (ctas == 0) return cudaSuccess;
+  if (D == 128) return launch_dense_pair_attention(p, maps, stream);
   if (D == 128) {
     const size_t smem = sizeof(FSmem<128>) + 1024;
     cudaError_t e = cudaFuncSetAttribute(flat_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));

@@ -104,6 +104,8 @@ struct AttnMaps {
 cudaError_t launch_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
 // Dense tiles of the flat query blocks, two 128-row tiles per CTA.
 cudaError_t launch_flat_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
+// Dense tiles of the flat query blocks for D = 128 on SM pairs (cta_group::2).
+cudaError_t launch_dense_pair_attention(const AttnParams& p, const AttnMaps& maps, cudaStream_t stream);
 // Block-sparse tiles (exact top_k blocks + interval term), P kept in TMEM.
 cudaError_t launch_sparse_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
 

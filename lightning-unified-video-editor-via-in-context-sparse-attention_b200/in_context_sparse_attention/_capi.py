@@ -20,6 +20,7 @@ STATUS = {0: "ICSA_OK", 1: "ICSA_ERR_INVALID", 2: "ICSA_ERR_UNSUPPORTED", 3: "IC
 
 EXPORTED = ("icsa_last_error", "icsa_version", "icsa_problem_init", "icsa_workspace_size",
             "icsa_get_workspace_layout", "icsa_forward", "icsa_pool", "icsa_select", "icsa_attend",
+            "icsa_attend_dense", "icsa_attend_sparse",
             "icsa_device_status")
 
 
@@ -90,6 +91,9 @@ def load(path: str = None) -> ctypes.CDLL:
         lib.icsa_select.restype = i
         lib.icsa_attend.argtypes = [pp, vp, vp, vp, vp, vp, vp, sz, vp]
         lib.icsa_attend.restype = i
+        for name in ("icsa_attend_dense", "icsa_attend_sparse"):
+            getattr(lib, name).argtypes = [pp, vp, vp, vp, vp, vp, vp, sz, vp]
+            getattr(lib, name).restype = i
         lib.icsa_device_status.argtypes = [vp, vp]
         lib.icsa_device_status.restype = i
         _lib = lib

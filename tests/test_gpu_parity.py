@@ -152,3 +152,28 @@ def test_device_status_clean(cuda_device):
     _, dbg = run_gpu(q, k, v, t)
     rc = _capi.load().icsa_device_status(dbg["workspace"].data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert rc == 0
+
+
+def test_stage_entry_points_equal_forward(cuda_device):
+    """pool -> select -> attend_dense -> attend_sparse (the timed path of the
+    benchmark) writes the same bytes as icsa_forward."""
+    import ctypes
+    from in_context_sparse_attention import _capi
+    lib = _capi.load()
+    B, S, H, D, t = 1, 4096, 2, 128, 2048
+    q, k, v = (x.cuda() for x in _rand(B, S, H, D, torch.bfloat16, seed=31, t=t))
+    p = _capi.problem(B, S, H, D, t)
+    pp = ctypes.byref(p)
+    size = lib.icsa_workspace_size(pp)
+    st = torch.cuda.current_stream().cuda_stream
+    a = (q.data_ptr(), k.data_ptr(), v.data_ptr())
+    ws1 = torch.empty(size, dtype=torch.uint8, device=q.device)
+    ws2 = torch.empty(size, dtype=torch.uint8, device=q.device)
+    out1, out2 = torch.empty_like(q), torch.empty_like(q)
+    _capi.check(lib.icsa_forward(pp, *a, None, out1.data_ptr(), ws1.data_ptr(), size, st), "icsa_forward")
+    _capi.check(lib.icsa_pool(pp, *a, ws2.data_ptr(), size, st), "icsa_pool")
+    _capi.check(lib.icsa_select(pp, a[1], a[2], ws2.data_ptr(), size, st), "icsa_select")
+    _capi.check(lib.icsa_attend_dense(pp, *a, None, out2.data_ptr(), ws2.data_ptr(), size, st), "dense")
+    _capi.check(lib.icsa_attend_sparse(pp, *a, None, out2.data_ptr(), ws2.data_ptr(), size, st), "sparse")
+    assert lib.icsa_device_status(ws2.data_ptr(), st) == 0
+    assert torch.equal(out1, out2)
