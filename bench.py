@@ -246,7 +246,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--cpu-heads", type=int, default=2, help="heads the CPU baseline runs in full")
+    ap.add_argument("--cpu-heads", type=int, default=8, help="heads the CPU baseline runs in full")
     ap.add_argument("--heads", type=int, default=0, help="run only this many heads (profiling of a small case)")
     args = ap.parse_args()
 
@@ -338,7 +338,7 @@ def main():
     achieved = flops / (stage["attend_dense"] * 1e-3) / 1e12
     sparse_achieved = sparse_flops / (stage["attend_sparse"] * 1e-3) / 1e12
     traffic = None
-    tpath = os.path.join(REPO, "profiles", "flat_kernel_traffic.json")
+    tpath = os.path.join(REPO, "profiles", "dense_pair_kernel_traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
             tr = json.load(f)
@@ -352,7 +352,7 @@ def main():
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded blurred-field generator)",
                 "config": config_dict(w, world),
                 "stages_ms": stage,
-                "roofline": {"bound": "tensor", "kernel": "flat_kernel (dense attention of the flat blocks)",
+                "roofline": {"bound": "tensor", "kernel": "dense_pair_kernel (dense attention of the flat blocks, SM pairs)",
                              "achieved": achieved, "peak": sustained, "unit": "TFLOP/s", "frac": achieved / sustained,
                              "peak_kind": f"{src} sustained bf16", "frac_of_burst": achieved / burst,
                              "traffic": traffic, "flops_per_launch": flops,
