@@ -183,6 +183,27 @@ ICSA_API int icsa_attend_sparse(const icsa_problem* p, const void* q, const void
                                 void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
+ * The whole call with q, k, v and the output in HOST memory (pinned for
+ * asynchronous copies), streamed through the current device by groups of
+ * `group_heads` heads (a divisor of H): the copy of one group to the device,
+ * the computation of another and the copy back of a third overlap on three
+ * streams.  Every stage of the reference is independent per (batch, head)
+ * (editing_sparse_attention.py:133-135,165-172; tilelang_kernels.py:802), so
+ * the result equals icsa_forward on device copies of the same inputs.  No
+ * counterpart in the reference, whose call takes device tensors.
+ *   alpha:     device pointer for ICSA_ALPHA_TENSOR (strides over [B,S,H,D]).
+ *   workspace: device memory of icsa_host_workspace_size() bytes, 256-byte
+ *              aligned; icsa_device_status(workspace, ...) reports device
+ *              timeouts of any group.
+ * Returns after enqueueing; `stream` completes when the whole output is in
+ * host memory.  Calls on one device are serialised by the library.
+ */
+ICSA_API size_t icsa_host_workspace_size(const icsa_problem* p, int group_heads);
+ICSA_API int icsa_forward_host(const icsa_problem* p, int group_heads, const void* q, const void* k, const void* v,
+                               const void* alpha, void* out, void* workspace, size_t workspace_bytes,
+                               cudaStream_t stream);
+
+/*
  * Synchronises `stream` and returns ICSA_OK or the status a device-side
  * bounded wait recorded in the workspace during the preceding calls.
  */

@@ -9,7 +9,11 @@ Same positional/keyword signature, same result shape and dtype rules:
                                  alpha_2=1.0, alpha_3=1.0, SPARSITY_RATIO=0.0625,
                                  backend='b200')
 
-* q, k, v: [B, S, H, D] CUDA tensors (bf16 or fp32), D in {64, 128}.
+* q, k, v: [B, S, H, D] CUDA tensors (bf16 or fp32), D in {64, 128}; or
+  pinned (page-locked) CPU tensors, which are streamed through the current
+  CUDA device by groups of heads (copy in, compute and copy out overlap on
+  three streams) and give a pinned CPU result.  Ordinary CPU tensors are
+  refused: there is no CPU fallback.
 * t_seq_len: target-video tokens.  s_seq_len and alpha_3 are accepted and
   unused, exactly as in the reference (only t_seq_len and S enter the
   computation).
@@ -24,9 +28,12 @@ Same positional/keyword signature, same result shape and dtype rules:
   hard-coded ``n_s // 8`` retrieved source blocks and ``NB // 2`` flat blocks
   (defaults reproduce them).
 
-The call is asynchronous on the current CUDA stream, performs no host
-synchronisation and allocates only its output and one workspace from the
-PyTorch caching allocator, so it can be captured in a CUDA graph.
+With CUDA inputs the call is asynchronous on the current CUDA stream,
+performs no host synchronisation and allocates only its output and one
+workspace from the PyTorch caching allocator, so it can be captured in a CUDA
+graph.  With pinned CPU inputs it returns once the result is in host memory,
+unless ``non_blocking=True`` (then synchronise the current stream before
+reading the result); ``out=`` takes a preallocated pinned result tensor.
 """
 from __future__ import annotations
 
@@ -69,13 +76,29 @@ def _result_dtypes(q_dtype, k_dtype, v_dtype, alpha):
     return outc, ca, out
 
 
+def _is_host(x) -> bool:
+    """True for a pinned CPU tensor (streamed through the GPU); raises for
+    any other non-CUDA tensor."""
+    if x.is_cuda:
+        return False
+    if x.device.type == "cpu" and x.is_pinned():
+        return True
+    raise RuntimeError(f"tensor is on {x.device}: the b200 backend computes on CUDA only (there is no CPU "
+                       "fallback); pass CUDA tensors, or pinned CPU tensors to stream them through the GPU")
+
+
+def _default_group_heads(H: int) -> int:
+    """Heads per streamed group: about eight groups, at least four heads per
+    group when H allows it (smaller groups leave SMs idle at the tail)."""
+    cap = max(4, H // 8)
+    return max(d for d in range(1, H + 1) if H % d == 0 and d <= cap)
+
+
 def _prepare(q, k, v, t_seq_len, alpha_2, SPARSITY_RATIO, select_ratio, flat_ratio, debug_keys=False):
     for name, x in (("q", q), ("k", k), ("v", v)):
         if not isinstance(x, torch.Tensor) or x.dim() != 4:
             raise ValueError(f"{name} must be a 4-D [B, S, H, D] tensor")
-        if not x.is_cuda:
-            raise RuntimeError(f"{name} is on {x.device}: the b200 backend runs on CUDA tensors only "
-                               "(there is no CPU fallback)")
+        _is_host(x)
         if x.dtype not in _DT:
             raise ValueError(f"{name} has dtype {x.dtype}; supported: bfloat16, float32")
     if q.shape != k.shape or q.shape[:3] != v.shape[:3] or v.shape[3] != q.shape[3]:
@@ -98,8 +121,9 @@ def _prepare(q, k, v, t_seq_len, alpha_2, SPARSITY_RATIO, select_ratio, flat_rat
         a = alpha_2
         if a.dtype not in _DT:
             a = a.float()
-        if a.device != q.device:
-            a = a.to(q.device)
+        dev = q.device if q.is_cuda else torch.device("cuda", torch.cuda.current_device())
+        if a.device != dev:
+            a = a.to(dev)
         a = a.expand(B, S, H, D) if a.dim() <= 4 else None
         if a is None:
             raise ValueError("alpha_2 must broadcast to [B, S, H, D]")
@@ -116,15 +140,53 @@ def _prepare(q, k, v, t_seq_len, alpha_2, SPARSITY_RATIO, select_ratio, flat_rat
     return p, out_dt, alpha_t
 
 
+def _streamed(lib, p, q, k, v, alpha_t, out_dt, out, group_heads, non_blocking):
+    """Pinned host q, k, v -> pinned host result through icsa_forward_host."""
+    B, S, H, D = q.shape
+    hg = group_heads or _default_group_heads(H)
+    if out is None:
+        out = torch.empty(B, S, H, D, dtype=out_dt, pin_memory=True)
+    elif (not isinstance(out, torch.Tensor) or out.shape != q.shape or out.dtype != out_dt or out.is_cuda
+          or not out.is_pinned() or not out.is_contiguous()):
+        raise ValueError(f"out must be a contiguous pinned CPU tensor of shape {tuple(q.shape)} and dtype {out_dt}")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(dev):
+        size = lib.icsa_host_workspace_size(ctypes.byref(p), hg)
+        if size == 0:
+            _capi.check(1, "icsa_host_workspace_size")
+        ws = torch.empty(size, dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        rc = lib.icsa_forward_host(ctypes.byref(p), hg, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                   alpha_t.data_ptr() if alpha_t is not None else None, out.data_ptr(),
+                                   ws.data_ptr(), size, stream.cuda_stream)
+        _capi.check(rc, "icsa_forward_host")
+        ws.record_stream(stream)
+        if not non_blocking:
+            stream.synchronize()
+    return out
+
+
 def editing_sparse_attention(q, k, v, t_seq_len, s_seq_len=None, alpha_2=1.0, alpha_3=1.0, SPARSITY_RATIO=0.0625,
-                             backend=Backend.B200, *, select_ratio=0.125, flat_ratio=0.5, _debug=None):
+                             backend=Backend.B200, *, select_ratio=0.125, flat_ratio=0.5, out=None,
+                             group_heads=None, non_blocking=False, _debug=None):
     """In-context sparse attention (see the module docstring).  Returns x
-    [B, S, H, D].  `_debug`, when a dict, receives the workspace and its
+    [B, S, H, D].  `out`, `group_heads` and `non_blocking` apply to pinned
+    CPU inputs only.  `_debug`, when a dict, receives the workspace and its
     layout (used by the parity tests to read selections and keys)."""
     Backend.validate(backend)
     lib = _capi.load()
     p, out_dt, alpha_t = _prepare(q, k, v, t_seq_len, alpha_2, SPARSITY_RATIO, select_ratio, flat_ratio,
                                   debug_keys=_debug is not None)
+    hosts = {_is_host(x) for x in (q, k, v)}
+    if len(hosts) != 1:
+        raise ValueError("q, k, v must all be CUDA tensors or all pinned CPU tensors")
+    if hosts.pop():
+        if _debug is not None:
+            raise ValueError("_debug is only available for CUDA inputs")
+        return _streamed(lib, p, q.contiguous(), k.contiguous(), v.contiguous(), alpha_t, out_dt, out, group_heads,
+                         non_blocking)
+    if out is not None:
+        raise ValueError("out= is only supported for pinned CPU inputs")
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     B, S, H, D = q.shape
     with torch.cuda.device(q.device):

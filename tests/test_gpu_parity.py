@@ -177,3 +177,29 @@ def test_stage_entry_points_equal_forward(cuda_device):
     _capi.check(lib.icsa_attend_sparse(pp, *a, None, out2.data_ptr(), ws2.data_ptr(), size, st), "sparse")
     assert lib.icsa_device_status(ws2.data_ptr(), st) == 0
     assert torch.equal(out1, out2)
+
+
+@pytest.mark.parametrize("group_heads", [None, 1, 3])
+def test_host_streaming_equals_device_call(cuda_device, group_heads):
+    """Pinned host inputs streamed by head groups give the same bytes as the
+    call on device copies (every stage is independent per head)."""
+    from in_context_sparse_attention import editing_sparse_attention
+    B, S, H, D, t = 1, 4096, 6, 128, 2048
+    q, k, v = _rand(B, S, H, D, torch.bfloat16, seed=41, t=t)
+    alpha = (torch.rand(B, S, 1, 1, generator=torch.Generator().manual_seed(7)) - 0.5)
+    want = editing_sparse_attention(q.cuda(), k.cuda(), v.cuda(), t, S - t, alpha_2=alpha.cuda()).cpu()
+    hq, hk, hv = (x.pin_memory() for x in (q, k, v))
+    got = editing_sparse_attention(hq, hk, hv, t, S - t, alpha_2=alpha.cuda(), group_heads=group_heads)
+    assert got.is_pinned() and got.dtype == want.dtype
+    assert torch.equal(got, want)
+    out = torch.empty_like(got).pin_memory()
+    again = editing_sparse_attention(hq, hk, hv, t, S - t, alpha_2=alpha.cuda(), out=out, non_blocking=True)
+    torch.cuda.current_stream().synchronize()
+    assert again is out and torch.equal(out, want)
+
+
+def test_unpinned_host_tensors_are_refused(cuda_device):
+    from in_context_sparse_attention import editing_sparse_attention
+    q = torch.randn(1, 128, 2, 64)
+    with pytest.raises(RuntimeError, match="no CPU"):
+        editing_sparse_attention(q, q, q, 64, 64)
