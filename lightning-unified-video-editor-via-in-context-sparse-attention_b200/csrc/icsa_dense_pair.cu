@@ -38,7 +38,7 @@ using namespace attn;
 constexpr int kPThreads = 384;
 constexpr int kPProducerWarp = 8;
 constexpr int kPMmaWarp = 9;
-constexpr int kPStages = 4;
+constexpr int kPStages = 5;  // K/V ring: stage j % 5 holds this CTA's halves of K(j) and V(j)
 constexpr int kPQBytes = 128 * 128 * 2;  // this CTA's 128 query rows, two 64-wide d chunks of 16 KB
 constexpr int kPKBytes = 64 * 128 * 2;   // 64 key rows x 128 d, two d chunks of 8 KB
 constexpr int kPVBytes = 128 * 64 * 2;   // 128 value rows x this CTA's 64 d
@@ -46,14 +46,12 @@ constexpr uint32_t kTmS = 0, kTmP = 256, kTmO = 384, kPTmemCols = 512;
 
 struct __align__(1024) PSmem {
   uint8_t q[kPQBytes];
-  uint8_t k[kPStages][kPKBytes];
-  uint8_t v[kPStages][kPVBytes];
+  uint8_t kv[kPStages][kPKBytes + kPVBytes];  // [K half | V half]
   float mref[2][128];  // [warpgroup][row] m_ref after that warpgroup's latest step
   float lsum[2][128];  // epilogue: partial row sums and their origins
   float lmax[2][128];
   uint64_t q_full;
-  uint64_t k_full[kPStages], k_empty[kPStages];
-  uint64_t v_full[kPStages], v_empty[kPStages];
+  uint64_t kv_full[kPStages], kv_empty[kPStages];
   uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
   uint64_t mma_fin;
   uint32_t tmem_base;
@@ -107,20 +105,18 @@ ICSA_DEV void pair_producer(const AttnParams& p, const AttnMaps& maps, const PTi
     const uint32_t ph = uint32_t(j / kPStages) & 1u;
     const int r0 = rows[2 * j];
     const int r1 = (2 * j + 1 < p.nkv) ? rows[2 * j + 1] : r0;  // missing half: masked by the softmax
+    if (!mbar_wait(&sm.kv_empty[s], ph ^ 1u, p.err, kErrKEmpty, abort_flag)) return;
+    if (leader) mbar_arrive_expect_tx(&sm.kv_full[s], 2 * (kPKBytes + kPVBytes));
+    const uint32_t kv_full = pair::mapa(&sm.kv_full[s], 0);
     // keys: this CTA's 64 of the 128 (N split)
-    if (!mbar_wait(&sm.k_empty[s], ph ^ 1u, p.err, kErrKEmpty, abort_flag)) return;
-    if (leader) mbar_arrive_expect_tx(&sm.k_full[s], 2 * kPKBytes);
-    const uint32_t k_full = pair::mapa(&sm.k_full[s], 0);
     const int rk = t.rank ? r1 : r0;
 #pragma unroll
     for (int c = 0; c < 2; ++c)
-      pair::tma_load_4d(sm.k[s] + c * (kPKBytes / 2), &maps.k, k_full, c * 64, t.h, rk, t.b);
+      pair::tma_load_4d(sm.kv[s] + c * (kPKBytes / 2), &maps.k, kv_full, c * 64, t.h, rk, t.b);
     // values: all 128 keys, this CTA's 64 of the 128 d (N split)
-    if (!mbar_wait(&sm.v_empty[s], ph ^ 1u, p.err, kErrVEmpty, abort_flag)) return;
-    if (leader) mbar_arrive_expect_tx(&sm.v_full[s], 2 * kPVBytes);
-    const uint32_t v_full = pair::mapa(&sm.v_full[s], 0);
-    pair::tma_load_4d(sm.v[s], &maps.v, v_full, int(t.rank) * 64, t.h, r0, t.b);
-    pair::tma_load_4d(sm.v[s] + kPVBytes / 2, &maps.v, v_full, int(t.rank) * 64, t.h, r1, t.b);
+    uint8_t* vdst = sm.kv[s] + kPKBytes;
+    pair::tma_load_4d(vdst, &maps.v, kv_full, int(t.rank) * 64, t.h, r0, t.b);
+    pair::tma_load_4d(vdst + kPVBytes / 2, &maps.v, kv_full, int(t.rank) * 64, t.h, r1, t.b);
   }
 }
 
@@ -154,37 +150,35 @@ ICSA_DEV void pair_mma(const AttnParams& p, const PTile& t, PSmem& sm, uint32_t 
   volatile int* abort_flag = &sm.abort_flag;
   const int n = t.n_steps;
   const uint64_t qd = tc::make_sw128_desc(smem_u32(sm.q), 16, 1024);
-  const uint64_t kd0 = tc::make_sw128_desc(smem_u32(sm.k[0]), 16, 1024);
-  const uint64_t vd0 = tc::make_sw128_desc(smem_u32(sm.v[0]), kPVBytes, 1024);
-  constexpr uint64_t kKStep = uint64_t(kPKBytes >> 4), kVStep = uint64_t(kPVBytes >> 4);
+  const uint64_t kd0 = tc::make_sw128_desc(smem_u32(sm.kv[0]), 16, 1024);
+  const uint64_t vd0 = tc::make_sw128_desc(smem_u32(sm.kv[0] + kPKBytes), kPVBytes, 1024);
+  constexpr uint64_t kKStep = uint64_t((kPKBytes + kPVBytes) >> 4), kVStep = kKStep;
   if (!warp_mbar_wait(&sm.q_full, 0, p.err, kErrQ, abort_flag)) return;
 
   auto issue_s = [&](int j) -> bool {
     const int s = j % kPStages;
-    if (!warp_mbar_wait(&sm.k_full[s], uint32_t(j / kPStages) & 1u, p.err, kErrKFull, abort_flag)) return false;
+    if (!warp_mbar_wait(&sm.kv_full[s], uint32_t(j / kPStages) & 1u, p.err, kErrKFull, abort_flag)) return false;
     tc::fence_after_sync();
     pair_issue_s_seq(qd, kd0 + uint64_t(s) * kKStep, tmem + kTmS + 128u * uint32_t(j & 1),
                      std::make_integer_sequence<int, 8>{});
     pair::commit_both_elect(&sm.s_full[j & 1]);
-    pair::commit_both_elect(&sm.k_empty[s]);
     return true;
   };
-
   auto issue_pv = [&](int j) -> bool {
     const int b = j & 1, s = j % kPStages;
     if (!warp_mbar_wait(&sm.p_full[b], uint32_t(j >> 1) & 1u, p.err, kErrPFull, abort_flag)) return false;
-    if (!warp_mbar_wait(&sm.v_full[s], uint32_t(j / kPStages) & 1u, p.err, kErrVFull, abort_flag)) return false;
     tc::fence_after_sync();
     pair_issue_pv_seq(vd0 + uint64_t(s) * kVStep, tmem + kTmP + 64u * uint32_t(b), tmem + kTmO, j > 0 ? 1u : 0u,
                       std::make_integer_sequence<int, 8>{});
     pair::commit_both_elect(&sm.pv_done[b]);
-    pair::commit_both_elect(&sm.v_empty[s]);
+    pair::commit_both_elect(&sm.kv_empty[s]);  // S(j) and P.V(j) have read stage s
     return true;
   };
 
   // S(j+2) is issued as soon as both CTAs' softmax has read S(j) (buffer j%2),
-  // P.V(j) once P(j) is written.  (Deferring P.V(j) behind S(j+3) measured
-  // slower: it delays the P buffer release.)
+  // P.V(j) once P(j) is written.  Issuing S further ahead of P.V (deferring
+  // P.V(j) behind S(j+3), or issuing whichever is ready first) measured
+  // slower: it delays the release of the P buffers.
   if (!issue_s(0)) return;
   if (n > 1 && !issue_s(1)) return;
   for (int j = 0; j < n; ++j) {
@@ -351,10 +345,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
     for (int i = 0; i < kPStages; ++i) {
-      mbar_init(&sm.k_full[i], 1);
-      mbar_init(&sm.k_empty[i], 1);
-      mbar_init(&sm.v_full[i], 1);
-      mbar_init(&sm.v_empty[i], 1);
+      mbar_init(&sm.kv_full[i], 1);
+      mbar_init(&sm.kv_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.s_full[i], 1);
@@ -398,8 +390,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         // the leader's full barriers count the bytes of both CTAs: let every
         // copy still in flight land before either CTA releases its memory
         for (int j = max(0, t.n_steps - kPStages); j < t.n_steps; ++j) {
-          drain_wait(&sm.k_full[j % kPStages], uint32_t(j / kPStages) & 1u, p.err);
-          drain_wait(&sm.v_full[j % kPStages], uint32_t(j / kPStages) & 1u, p.err);
+          drain_wait(&sm.kv_full[j % kPStages], uint32_t(j / kPStages) & 1u, p.err);
         }
         drain_wait(&sm.q_full, 0, p.err);
       }
