@@ -10,13 +10,13 @@
 // writes), under the 128 B/clk the tensor core can draw from it.
 //
 // TMEM (512 columns per CTA):
-//   S(j) in buffer j%2 at [0,128) / [128,256)   fp32 scores, lane = query row
-//   P(j) in buffer j%2 at [256,320) / [320,384) bf16 pairs (A operand of P.V)
-//   O at [384,512)                               fp32 accumulator
-// Because P has its own columns, S(j+2) may overwrite S buffer j%2 as soon as
-// the softmax has copied S(j) to registers; the softmax never waits for its
-// own P.V, and the tensor core works from a queue filled two steps ahead:
-//   S(0) S(1) | S(j+2) after softmax(j) read S(j), P.V(j) after P(j) | ...
+//   S at [0,128)                                  fp32 scores, lane = query row
+//   P(j) in buffer j%4 at [128 + 64 (j%4), +64)   bf16 pairs (A operand of P.V)
+//   O at [384,512)                                fp32 accumulator
+// Because P has its own columns, S(j+1) may overwrite S as soon as the
+// softmax has copied S(j) to registers, and with four P buffers P(j) never
+// waits for a recent P.V.  The tensor core's queue per step:
+//   S(j+1) once softmax(j) has read S(j), then P.V(j-1) once P(j-1) is written.
 //
 // Roles per CTA (384 threads):
 //   warps 0-3 / 4-7  softmax of key columns [0,64) / [64,128) of every row
@@ -42,7 +42,7 @@ constexpr int kPStages = 5;  // K/V ring: stage j % 5 holds this CTA's halves of
 constexpr int kPQBytes = 128 * 128 * 2;  // this CTA's 128 query rows, two 64-wide d chunks of 16 KB
 constexpr int kPKBytes = 64 * 128 * 2;   // 64 key rows x 128 d, two d chunks of 8 KB
 constexpr int kPVBytes = 128 * 64 * 2;   // 128 value rows x this CTA's 64 d
-constexpr uint32_t kTmS = 0, kTmP = 256, kTmO = 384, kPTmemCols = 512;
+constexpr uint32_t kTmS = 0, kTmP = 128, kTmO = 384, kPTmemCols = 512;
 
 struct __align__(1024) PSmem {
   uint8_t q[kPQBytes];
@@ -52,7 +52,11 @@ struct __align__(1024) PSmem {
   float lmax[2][128];
   uint64_t q_full;
   uint64_t kv_full[kPStages], kv_empty[kPStages];
-  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  // [w]: barriers of softmax warpgroup w (steps j with j % 2 == w), so each
+  // is consumed in phase order by one party
+  uint64_t s_full[2], s_free[2], p_full[2];
+  uint64_t pv_done[4];  // P.V(j) done, per P buffer j % 4
+  uint64_t o_final;     // the last P.V done
   uint64_t mma_fin;
   uint32_t tmem_base;
   int abort_flag;
@@ -159,35 +163,34 @@ ICSA_DEV void pair_mma(const AttnParams& p, const PTile& t, PSmem& sm, uint32_t 
     const int s = j % kPStages;
     if (!warp_mbar_wait(&sm.kv_full[s], uint32_t(j / kPStages) & 1u, p.err, kErrKFull, abort_flag)) return false;
     tc::fence_after_sync();
-    pair_issue_s_seq(qd, kd0 + uint64_t(s) * kKStep, tmem + kTmS + 128u * uint32_t(j & 1),
-                     std::make_integer_sequence<int, 8>{});
+    pair_issue_s_seq(qd, kd0 + uint64_t(s) * kKStep, tmem + kTmS, std::make_integer_sequence<int, 8>{});
     pair::commit_both_elect(&sm.s_full[j & 1]);
     return true;
   };
   auto issue_pv = [&](int j) -> bool {
-    const int b = j & 1, s = j % kPStages;
-    if (!warp_mbar_wait(&sm.p_full[b], uint32_t(j >> 1) & 1u, p.err, kErrPFull, abort_flag)) return false;
+    const int s = j % kPStages;
+    if (!warp_mbar_wait(&sm.p_full[j & 1], uint32_t(j >> 1) & 1u, p.err, kErrPFull, abort_flag)) return false;
     tc::fence_after_sync();
-    pair_issue_pv_seq(vd0 + uint64_t(s) * kVStep, tmem + kTmP + 64u * uint32_t(b), tmem + kTmO, j > 0 ? 1u : 0u,
+    pair_issue_pv_seq(vd0 + uint64_t(s) * kVStep, tmem + kTmP + 64u * uint32_t(j & 3), tmem + kTmO, j > 0 ? 1u : 0u,
                       std::make_integer_sequence<int, 8>{});
-    pair::commit_both_elect(&sm.pv_done[b]);
+    pair::commit_both_elect(&sm.pv_done[j & 3]);
     pair::commit_both_elect(&sm.kv_empty[s]);  // S(j) and P.V(j) have read stage s
     return true;
   };
 
-  // S(j+2) is issued as soon as both CTAs' softmax has read S(j) (buffer j%2),
-  // P.V(j) once P(j) is written.  Issuing S further ahead of P.V (deferring
-  // P.V(j) behind S(j+3), or issuing whichever is ready first) measured
-  // slower: it delays the release of the P buffers.
+  // The softmax warpgroups run half a step apart, so s_free(j) (early in
+  // softmax j) and p_full(j-1) (end of softmax j-1) alternate:
+  //   S(j+1) after s_free(j), P.V(j-1) after p_full(j-1).
   if (!issue_s(0)) return;
-  if (n > 1 && !issue_s(1)) return;
   for (int j = 0; j < n; ++j) {
-    if (j + 2 < n) {
+    if (j + 1 < n) {
       if (!warp_mbar_wait(&sm.s_free[j & 1], uint32_t(j >> 1) & 1u, p.err, kErrSEmpty, abort_flag)) return;
-      if (!issue_s(j + 2)) return;
+      if (!issue_s(j + 1)) return;
     }
-    if (!issue_pv(j)) return;
+    if (j > 0 && !issue_pv(j - 1)) return;
   }
+  if (!issue_pv(n - 1)) return;
+  pair::commit_both_elect(&sm.o_final);
 }
 
 // Softmax: warpgroup w handles the key steps j with j % 2 == w, over all 128
@@ -212,8 +215,8 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const PTile& t, PSmem& sm, uint3
   const uint32_t bar_to_other = 1u + 4u * uint32_t(w) + uint32_t(warp & 3);
   const uint32_t bar_from_other = 1u + 4u * uint32_t(w ^ 1) + uint32_t(warp & 3);
   const uint32_t lanes = uint32_t((warp & 3) * 32) << 16;
-  const uint32_t s_base = tmem + lanes + kTmS + 128u * uint32_t(w);
-  const uint32_t p_base = tmem + lanes + kTmP + 64u * uint32_t(w);
+  const uint32_t s_base = tmem + lanes + kTmS;
+  const uint32_t p_base = tmem + lanes + kTmP + 64u * uint32_t(w);  // + 128 for odd own steps
   const uint32_t o_base = tmem + lanes + kTmO;
   const uint32_t s_free = pair::mapa(&sm.s_free[w], 0);
   const uint32_t p_full = pair::mapa(&sm.p_full[w], 0);
@@ -227,7 +230,7 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const PTile& t, PSmem& sm, uint3
     tc::fence_after_sync();
     float s[128];
     tmem_load_row128(s_base, s);
-    // S buffer w may now be overwritten by S(j+2)
+    // S may now be overwritten by S(j+1)
     tc::fence_before_sync();
     __syncwarp();
     if (lane == 0) pair::arrive_cluster_relaxed(s_free);
@@ -255,8 +258,10 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const PTile& t, PSmem& sm, uint3
       l_w = (m_w == -INFINITY) ? 0.f : l_w * ex2((m_w - m_ref) * sl2);
       m_w = m_ref;
     }
-    // P buffer w was last read by P.V(j-2)
-    if (j >= 2) warp_mbar_wait(&sm.pv_done[w], uint32_t((j - 2) >> 1) & 1u, p.err, kErrPvDone, abort_flag);
+    // P buffer j%4 was last read by P.V(j-4) (issued before S(j), so in
+    // practice already complete)
+    const int pb = j & 3;
+    if (j >= 4) warp_mbar_wait(&sm.pv_done[pb], uint32_t((j - 4) >> 2) & 1u, p.err, kErrPvDone, abort_flag);
     tc::fence_after_sync();
     const float neg = -m_ref * sl2;
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
@@ -275,13 +280,15 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const PTile& t, PSmem& sm, uint3
         uint32_t pk[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) pk[e] = pack_bf16x2(s[(c & ~63) + 2 * e], s[(c & ~63) + 2 * e + 1]);
-        tc::tmem_st32(p_base + uint32_t(c >> 6) * 32u, pk);
+        tc::tmem_st32(p_base + 128u * uint32_t(pb >> 1) + uint32_t(c >> 6) * 32u, pk);
       }
     }
     l_w += (a0 + a1) + (a2 + a3);
     if (j > 0 && __any_sync(0xffffffffu, need)) {
-      // O holds P.V up to step j-1 relative to m_prev: rescale it to m_ref
-      warp_mbar_wait(&sm.pv_done[w ^ 1], uint32_t((j - 1) >> 1) & 1u, p.err, kErrPvDone, abort_flag);
+      // O holds P.V up to step j-1 relative to m_prev: rescale it to m_ref.
+      // The phase before P.V(j-1) on its barrier is P.V(j-5), issued before
+      // S(j), which has completed, so the parity wait is exact.
+      warp_mbar_wait(&sm.pv_done[(j - 1) & 3], uint32_t((j - 1) >> 2) & 1u, p.err, kErrPvDone, abort_flag);
       tc::fence_after_sync();
       const float alpha = need ? ex2((m_prev - m_ref) * sl2) : 1.f;
 #pragma unroll 1
@@ -304,7 +311,7 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const PTile& t, PSmem& sm, uint3
   // epilogue: both partial sums to the final origin; this warpgroup writes
   // features [64w, 64w + 64) of its row
   const int last = n - 1;
-  warp_mbar_wait(&sm.pv_done[last & 1], uint32_t(last >> 1) & 1u, p.err, kErrPvDone, abort_flag);
+  warp_mbar_wait(&sm.o_final, 0, p.err, kErrPvDone, abort_flag);
   tc::fence_after_sync();
   sm.lsum[w][row] = l_w;
   sm.lmax[w][row] = m_w;
@@ -350,10 +357,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.pv_done[i], 1);
       mbar_init(&sm.s_free[i], 8);  // one arrival per warp of the step's warpgroup, both CTAs
       mbar_init(&sm.p_full[i], 8);
     }
+    for (int i = 0; i < 4; ++i) mbar_init(&sm.pv_done[i], 1);
+    mbar_init(&sm.o_final, 1);
     mbar_init(&sm.mma_fin, 1);
     sm.abort_flag = 0;
     fence_mbarrier_init();
