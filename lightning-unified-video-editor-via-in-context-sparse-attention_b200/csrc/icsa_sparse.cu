@@ -27,6 +27,8 @@
 // core computes the next scores while the softmax of step j runs.
 #include "icsa_attn_common.cuh"
 
+#include <utility>
+
 namespace icsa {
 
 namespace {
@@ -136,59 +138,65 @@ ICSA_DEV void sparse_producer(const AttnParams& p, const AttnMaps& maps, const S
   }
 }
 
-template <int D>
-ICSA_DEV void sparse_issue_s(SSmem<D>& sm, uint32_t tmem, int j) {
+// Descriptor offsets of the K steps (16 bf16 = 32 bytes inside a 128-byte
+// swizzled row; the next 64-wide chunk of d is 16 KB further), added inside
+// the instruction block so that no per-step descriptor is built.
+template <int KK>
+constexpr uint32_t kSparseSOff = uint32_t(((KK >> 2) * kChunkBytes + (KK & 3) * 32) >> 4);
+
+template <int... KK>
+ICSA_DEV void sparse_issue_s_seq(uint64_t q_desc, uint64_t k_desc, uint32_t d_tmem, std::integer_sequence<int, KK...>) {
   constexpr uint32_t idesc = tc::make_idesc_bf16(128, 128, false, false);
-  const uint32_t q_addr = smem_u32(sm.q);
-  const uint32_t k_addr = smem_u32(sm.k[j % SCfg<D>::kStages]);
-#pragma unroll
-  for (int kk = 0; kk < D / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * kChunkBytes + (kk & 3) * 32;
-    tc::mma_bf16_ss(tmem + (j & 1) * 128, tc::make_sw128_desc(q_addr + off, 16, 1024),
-                    tc::make_sw128_desc(k_addr + off, 16, 1024), idesc, kk > 0 ? 1u : 0u);
-  }
+  (tc::mma_bf16_ss_elect<kSparseSOff<KK>, kSparseSOff<KK>>(d_tmem, q_desc, k_desc, idesc, KK > 0 ? 1u : 0u), ...);
 }
 
-template <int D>
-ICSA_DEV void sparse_issue_pv(SSmem<D>& sm, uint32_t tmem, int j, uint32_t acc_col, bool accumulate) {
+// P.V: 128 KV rows, 16 per instruction; P occupies 8 TMEM columns per step,
+// V (MN-major) advances 16 rows = 2048 bytes.
+template <int D, int... KK>
+ICSA_DEV void sparse_issue_pv_seq(uint64_t v_desc, uint32_t p_tmem, uint32_t o_tmem, uint32_t acc,
+                                  std::integer_sequence<int, KK...>) {
   constexpr uint32_t idesc = tc::make_idesc_bf16(128, D, false, true);
-  const uint32_t v_addr = smem_u32(sm.v[j % SCfg<D>::kStages]);
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk)
-    tc::mma_bf16_ts(tmem + acc_col, tmem + (j & 1) * 128 + kk * 8,
-                    tc::make_sw128_desc(v_addr + kk * 16 * 128, kChunkBytes, 1024), idesc,
-                    (accumulate || kk > 0) ? 1u : 0u);
+  (tc::mma_bf16_ts_elect<uint32_t(KK * 8), uint32_t((KK * 16 * 128) >> 4)>(o_tmem, p_tmem, v_desc, idesc,
+                                                                           (KK > 0) ? 1u : acc),
+   ...);
 }
 
+// MMA issuer: all 32 lanes of warp 5 run this loop (waits are warp-uniform,
+// one elected lane issues each instruction).
 template <int D>
 ICSA_DEV void sparse_mma(const AttnParams& p, const STile& t, SSmem<D>& sm, uint32_t tmem) {
   using C = SCfg<D>;
   volatile int* abort_flag = &sm.abort_flag;
   const int n = t.n_steps;
-  if (!mbar_wait(&sm.q_full, 0, p.err, kErrQ, abort_flag)) return;
-  if (!mbar_wait(&sm.k_full[0], 0, p.err, kErrKFull, abort_flag)) return;
-  tc::fence_after_sync();
-  sparse_issue_s<D>(sm, tmem, 0);
-  tc::mma_commit(&sm.s_full[0]);
-  tc::mma_commit(&sm.k_empty[0]);
-  for (int j = 0; j < n; ++j) {
-    if (j + 1 < n) {
-      // S(j+1) goes to the buffer of P(j-1), whose P.V was issued before
-      const int st = (j + 1) % C::kStages;
-      if (!mbar_wait(&sm.k_full[st], uint32_t((j + 1) / C::kStages) & 1u, p.err, kErrKFull, abort_flag)) return;
-      tc::fence_after_sync();
-      sparse_issue_s<D>(sm, tmem, j + 1);
-      tc::mma_commit(&sm.s_full[(j + 1) & 1]);
-      tc::mma_commit(&sm.k_empty[st]);
-    }
+  const uint64_t qd = tc::make_sw128_desc(smem_u32(sm.q), 16, 1024);
+  const uint64_t kd0 = tc::make_sw128_desc(smem_u32(sm.k[0]), 16, 1024);
+  const uint64_t vd0 = tc::make_sw128_desc(smem_u32(sm.v[0]), kChunkBytes, 1024);
+  constexpr uint64_t kStageStep = uint64_t(C::kOpBytes >> 4);
+  if (!warp_mbar_wait(&sm.q_full, 0, p.err, kErrQ, abort_flag)) return;
+  auto issue_s = [&](int j) -> bool {
     const int st = j % C::kStages;
-    if (!mbar_wait(&sm.v_full[st], uint32_t(j / C::kStages) & 1u, p.err, kErrVFull, abort_flag)) return;
-    if (!mbar_wait(&sm.p_full[j & 1], uint32_t(j >> 1) & 1u, p.err, kErrPFull, abort_flag)) return;
+    if (!warp_mbar_wait(&sm.k_full[st], uint32_t(j / C::kStages) & 1u, p.err, kErrKFull, abort_flag)) return false;
+    tc::fence_after_sync();
+    sparse_issue_s_seq(qd, kd0 + uint64_t(st) * kStageStep, tmem + uint32_t(j & 1) * 128u,
+                       std::make_integer_sequence<int, D / 16>{});
+    tc::mma_commit_elect(&sm.s_full[j & 1]);
+    tc::mma_commit_elect(&sm.k_empty[st]);
+    return true;
+  };
+  if (!issue_s(0)) return;
+  for (int j = 0; j < n; ++j) {
+    // S(j+1) goes to the buffer of P(j-1), whose P.V was issued before
+    if (j + 1 < n && !issue_s(j + 1)) return;
+    const int st = j % C::kStages;
+    if (!warp_mbar_wait(&sm.v_full[st], uint32_t(j / C::kStages) & 1u, p.err, kErrVFull, abort_flag)) return;
+    if (!warp_mbar_wait(&sm.p_full[j & 1], uint32_t(j >> 1) & 1u, p.err, kErrPFull, abort_flag)) return;
     tc::fence_after_sync();
     const bool interval = j >= t.n_exact;
-    sparse_issue_pv<D>(sm, tmem, j, interval ? kSColG : kSColO, interval ? (j > t.n_exact) : (j > 0));
-    tc::mma_commit(&sm.pv_done);
-    tc::mma_commit(&sm.v_empty[st]);
+    const uint32_t acc = interval ? (j > t.n_exact) : (j > 0);
+    sparse_issue_pv_seq<D>(vd0 + uint64_t(st) * kStageStep, tmem + uint32_t(j & 1) * 128u,
+                           tmem + (interval ? kSColG : kSColO), acc ? 1u : 0u, std::make_integer_sequence<int, 8>{});
+    tc::mma_commit_elect(&sm.pv_done);
+    tc::mma_commit_elect(&sm.v_empty[st]);
   }
 }
 
@@ -411,11 +419,9 @@ __global__ void __launch_bounds__(kSThreads, 1) sparse_kernel(const AttnParams p
       }
     }
   } else {
-    if (lane == 0) {
-      sparse_mma<D>(p, t, sm, tmem);
-      tc::mma_commit(&sm.mma_fin);
-      drain_wait(&sm.mma_fin, 0, p.err);
-    }
+    sparse_mma<D>(p, t, sm, tmem);
+    tc::mma_commit_elect(&sm.mma_fin);
+    if (lane == 0) drain_wait(&sm.mma_fin, 0, p.err);
   }
   tc::fence_before_sync();
   __syncthreads();

@@ -99,6 +99,44 @@ ICSA_DEV void mma_bf16_ts_off(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
       : "memory");
 }
 
+// Warp-converged forms: every lane of the issuing warp executes them and the
+// lane chosen by elect.sync issues.  A converged issuing warp keeps the
+// descriptor arithmetic warp-uniform, which issues much faster than a single
+// diverged lane.
+template <uint32_t AOFF, uint32_t BOFF>
+ICSA_DEV void mma_bf16_ss_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b64 ta, tb;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "add.s64 ta, %1, %5;\n\t"
+      "add.s64 tb, %2, %6;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ta, tb, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(AOFF), "n"(BOFF)
+      : "memory");
+}
+template <uint32_t AOFF, uint32_t BOFF>
+ICSA_DEV void mma_bf16_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 ta;\n\t.reg .b64 tb;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "add.s32 ta, %1, %5;\n\t"
+      "add.s64 tb, %2, %6;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], tb, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(AOFF), "n"(BOFF)
+      : "memory");
+}
+ICSA_DEV void mma_commit_elect(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
 // Arrive (once) on an mbarrier when all previously issued tcgen05.mma of this
 // thread have completed.
 ICSA_DEV void mma_commit(uint64_t* bar) {
