@@ -40,6 +40,7 @@ constexpr int kSProducerWarp = 4;
 constexpr int kSMmaWarp = 5;
 constexpr uint32_t kSTmemCols = 512;
 constexpr uint32_t kSColO = 256, kSColG = 384;
+constexpr int kSMaskWords = 64;  // masks of up to 2048 extended-KV blocks are staged in shared memory
 
 template <int D>
 struct SCfg {
@@ -56,6 +57,8 @@ struct __align__(1024) SSmem {
   uint64_t q_full;
   uint64_t k_full[SCfg<D>::kStages], k_empty[SCfg<D>::kStages];
   uint64_t v_full[SCfg<D>::kStages], v_empty[SCfg<D>::kStages];
+  float outc[2][D];                       // out_compress rows of the tile's two query blocks
+  uint32_t mask[2][kSMaskWords];          // their selection bit masks (when nkv_pad <= 32 * kSMaskWords)
   uint64_t s_full[2], p_full[2], pv_done;  // p_full per S buffer: the softmax may run one step ahead
   uint64_t mma_fin;
   uint32_t tmem_base;
@@ -216,6 +219,10 @@ ICSA_DEV float max64(const float (&s)[64]) {
   return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
 }
 
+// The four softmax warps meet at named barrier 1 (staged masks and
+// out_compress), so none may leave early: after a failed wait the abort flag
+// is set, later waits return at once, the loop runs on over stale data and
+// the error code marks the result invalid.
 template <int D>
 ICSA_DEV void sparse_softmax(const AttnParams& p, const STile& t, SSmem<D>& sm, uint32_t tmem) {
   volatile int* abort_flag = &sm.abort_flag;
@@ -226,14 +233,31 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const STile& t, SSmem<D>& sm, 
   const float sl2 = p.scale_log2;
   const int n = t.n_steps;
   const int words = p.nkv_pad / 32;
-  const uint32_t* mask_row = p.sel_mask + (size_t(t.bh) * p.n_sparse + (half ? t.rank[1] : t.rank[0])) * words;
+  // Stage what the interval steps and the epilogue read (masks, out_compress)
+  // in shared memory; the loads are issued now and land while the exact
+  // steps run.  The four softmax warps meet at named barrier 1 before use.
+  const bool mask_in_smem = words <= kSMaskWords;
+  {
+    const int hb = tid >> 6, i = tid & 63;
+    const int rk = hb ? t.rank[1] : t.rank[0];
+    const int bk = hb ? t.blk[1] : t.blk[0];
+    const float* oc_src = p.outc + (size_t(t.bh) * p.NB + bk) * D;
+    for (int d = i; d < D; d += 64) sm.outc[hb][d] = oc_src[d];
+    if (mask_in_smem) {
+      const uint32_t* msrc = p.sel_mask + (size_t(t.bh) * p.n_sparse + rk) * words;
+      for (int w = i; w < words; w += 64) sm.mask[hb][w] = msrc[w];
+    }
+  }
+  const uint32_t* mask_row = mask_in_smem ? sm.mask[half]
+                                          : p.sel_mask + (size_t(t.bh) * p.n_sparse + (half ? t.rank[1] : t.rank[0])) * words;
+  bool staged = false;
   float m_ref = -INFINITY;   // exponent origin of O and l (raw score units)
   float m_true = -INFINITY;  // running max as the reference tracks it
   float l = 0.f, g_l = 0.f;
 
   for (int j = 0; j < n; ++j) {
     const int sb = j & 1;
-    if (!warp_mbar_wait(&sm.s_full[sb], uint32_t(j >> 1) & 1u, p.err, kErrSFull, abort_flag)) return;
+    warp_mbar_wait(&sm.s_full[sb], uint32_t(j >> 1) & 1u, p.err, kErrSFull, abort_flag);
     tc::fence_after_sync();
     const uint32_t s_col = tmem + lanes + sb * 128;
     if (j < t.n_exact) {
@@ -271,7 +295,7 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const STile& t, SSmem<D>& sm, 
       }
       l += (a0 + a1) + (a2 + a3);
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        if (!warp_mbar_wait(&sm.pv_done, uint32_t(j - 1) & 1u, p.err, kErrPvDone, abort_flag)) return;
+        warp_mbar_wait(&sm.pv_done, uint32_t(j - 1) & 1u, p.err, kErrPvDone, abort_flag);
         tc::fence_after_sync();
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -292,6 +316,10 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const STile& t, SSmem<D>& sm, 
       tc::tmem_st32(s_col + half * 32, pk);
       tc::tmem_st32(s_col + (1 - half) * 32, zero);
     } else {
+      if (!staged) {
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        staged = true;
+      }
       // interval step: two BN=64 chunks of pooled blocks, all 128 columns
       float s[128];
       tmem_load_row128(s_col, s);
@@ -340,15 +368,16 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const STile& t, SSmem<D>& sm, 
   }
 
   // epilogue: (acc * f + g_acc) / (l * f + g_l), f re-bases acc and l on the final max
-  if (!warp_mbar_wait(&sm.pv_done, uint32_t(n - 1) & 1u, p.err, kErrPvDone, abort_flag)) return;
+  warp_mbar_wait(&sm.pv_done, uint32_t(n - 1) & 1u, p.err, kErrPvDone, abort_flag);
   tc::fence_after_sync();
+  if (!staged) asm volatile("bar.sync 1, 128;" ::: "memory");
   const float f = ex2((m_ref - m_true) * sl2);
   const float denom = l * f + g_l;
   const float inv = denom == 0.f ? 0.f : 1.0f / denom;  // the reference's guard: 0 where the denominator is 0
   const int blk = half ? t.blk[1] : t.blk[0];
   const int token = blk * kBlock + (tid & 63);
   const bool write = (half == 0 || t.write1) && token < p.S;
-  const float* oc = p.outc + (size_t(t.bh) * p.NB + blk) * D;
+  const float* oc = sm.outc[half];
   const size_t out_row = ((size_t(t.b) * p.S + token) * p.H + t.h) * D;
 #pragma unroll 1
   for (int c = 0; c < D / 32; ++c) {
