@@ -23,47 +23,56 @@ namespace {
 
 // ---------------------------------------------------------------------------
 // scores[bh, i, j] = dot(qmean[bh, i], kmean[bh, j]) / sqrt(D)
-// 64x64 output tile per CTA, 256 threads, 4x4 outputs per thread.
+// 128x128 output tile per CTA, 256 threads, 8x8 outputs per thread (rows and
+// columns split into two groups of 4, 64 apart, so that the float4 reads of
+// shared memory are conflict-free).  Every output accumulates over k in
+// increasing order with fmaf, then divides by sqrt(D).
 // ---------------------------------------------------------------------------
-constexpr int kGT = 64;   // GEMM tile
-constexpr int kGK = 16;   // GEMM k-chunk
+constexpr int kGT = 128;  // GEMM tile
+constexpr int kGK = 8;    // GEMM k-chunk
 
 __global__ void __launch_bounds__(256) scores_kernel(SelectParams p) {
-  __shared__ float As[kGK][kGT + 4];
-  __shared__ float Bs[kGK][kGT + 4];
+  __shared__ __align__(16) float As[kGK][kGT + 4];
+  __shared__ __align__(16) float Bs[kGK][kGT + 4];
   const int bh = blockIdx.z;
   const int i0 = blockIdx.y * kGT, j0 = blockIdx.x * kGT;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
   const float* A = p.qmean + size_t(bh) * p.NB * p.D;
   const float* Bm = p.kmean + size_t(bh) * p.NB * p.D;
-  float acc[4][4] = {};
+  const int lr = threadIdx.x >> 1, lk = (threadIdx.x & 1) * 4;  // loader: row, first k of a float4
+  float acc[8][8] = {};
   for (int k0 = 0; k0 < p.D; k0 += kGK) {
-    for (int e = threadIdx.x; e < kGT * kGK; e += 256) {
-      const int r = e / kGK, c = e % kGK;
-      As[c][r] = (i0 + r < p.NB) ? A[size_t(i0 + r) * p.D + k0 + c] : 0.f;
-      Bs[c][r] = (j0 + r < p.NB) ? Bm[size_t(j0 + r) * p.D + k0 + c] : 0.f;
+    {
+      const float4 za = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 va = (i0 + lr < p.NB) ? *reinterpret_cast<const float4*>(A + size_t(i0 + lr) * p.D + k0 + lk) : za;
+      const float4 vb = (j0 + lr < p.NB) ? *reinterpret_cast<const float4*>(Bm + size_t(j0 + lr) * p.D + k0 + lk) : za;
+      As[lk + 0][lr] = va.x; As[lk + 1][lr] = va.y; As[lk + 2][lr] = va.z; As[lk + 3][lr] = va.w;
+      Bs[lk + 0][lr] = vb.x; Bs[lk + 1][lr] = vb.y; Bs[lk + 2][lr] = vb.z; Bs[lk + 3][lr] = vb.w;
     }
     __syncthreads();
 #pragma unroll
     for (int c = 0; c < kGK; ++c) {
-      float a[4], b[4];
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[c][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[c][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[c][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[c][64 + tx * 4]);
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-      for (int u = 0; u < 4; ++u) { a[u] = As[c][ty * 4 + u]; b[u] = Bs[c][tx * 4 + u]; }
+      for (int u = 0; u < 8; ++u)
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-#pragma unroll
-        for (int w = 0; w < 4; ++w) acc[u][w] = fmaf(a[u], b[w], acc[u][w]);
+        for (int w = 0; w < 8; ++w) acc[u][w] = fmaf(a[u], b[w], acc[u][w]);
     }
     __syncthreads();
   }
   float* S = p.scores + size_t(bh) * p.NB * p.NB;
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int i = i0 + ty * 4 + u;
+  for (int u = 0; u < 8; ++u) {
+    const int i = i0 + (u < 4 ? ty * 4 + u : 64 + ty * 4 + u - 4);
     if (i >= p.NB) continue;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const int j = j0 + tx * 4 + w;
+    for (int w = 0; w < 8; ++w) {
+      const int j = j0 + (w < 4 ? tx * 4 + w : 64 + tx * 4 + w - 4);
       if (j < p.NB) S[size_t(i) * p.NB + j] = acc[u][w] / p.inv_sqrt_d_div;
     }
   }
@@ -120,53 +129,83 @@ __global__ void rowstats_kernel(SelectParams p, int warps, int stride) {
 
 // ---------------------------------------------------------------------------
 // out_c[bh, i, :] = sum_j P[i, j] * vmean[bh, j, :],  P = exp(s - m) / l.
+// A CTA owns 64 rows and all D columns, so each probability is computed once
+// (2^((s - m) log2 e) times 1/l); chunks of 32 columns of P and rows of V are
+// staged in shared memory.  256 threads, 4 rows x D/16 columns per thread.
 // ---------------------------------------------------------------------------
+constexpr int kOR = 64;   // rows per CTA
+constexpr int kOJ = 32;   // j per chunk
+
+ICSA_DEV float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D>
 __global__ void __launch_bounds__(256) outc_kernel(SelectParams p) {
-  __shared__ float Ps[kGK][kGT + 4];
-  __shared__ float Vs[kGK][kGT + 4];
-  __shared__ float sm[kGT], sl[kGT];
-  const int bh = blockIdx.z;
-  const int i0 = blockIdx.y * kGT, d0 = blockIdx.x * kGT;
+  constexpr int kCW = D / 16;  // columns per thread: D/64 groups of 4, 64 apart
+  __shared__ __align__(16) float Ps[kOJ][kOR + 4];
+  __shared__ __align__(16) float Vs[kOJ][D + 4];
+  __shared__ float sm[kOR], sl[kOR];
+  const int bh = blockIdx.y;
+  const int i0 = blockIdx.x * kOR;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
   const float* S = p.scores + size_t(bh) * p.NB * p.NB;
-  const float* V = p.vmean + size_t(bh) * p.NB * p.D;
-  if (threadIdx.x < kGT) {
+  const float* V = p.vmean + size_t(bh) * p.NB * D;
+  constexpr float kLog2e = 1.4426950408889634f;
+  if (threadIdx.x < kOR) {
     const int i = i0 + threadIdx.x;
-    sm[threadIdx.x] = (i < p.NB) ? p.rowmax[size_t(bh) * p.NB + i] : 0.f;
-    sl[threadIdx.x] = (i < p.NB) ? p.rowsum[size_t(bh) * p.NB + i] : 1.f;
+    sm[threadIdx.x] = (i < p.NB) ? p.rowmax[size_t(bh) * p.NB + i] * kLog2e : 0.f;
+    sl[threadIdx.x] = (i < p.NB) ? 1.0f / p.rowsum[size_t(bh) * p.NB + i] : 0.f;
   }
   __syncthreads();
-  float acc[4][4] = {};
-  for (int j0 = 0; j0 < p.NB; j0 += kGK) {
-    for (int e = threadIdx.x; e < kGT * kGK; e += 256) {
-      const int r = e / kGK, c = e % kGK;
-      const int i = i0 + r, j = j0 + c;
-      Ps[c][r] = (i < p.NB && j < p.NB) ? expf(S[size_t(i) * p.NB + j] - sm[r]) / sl[r] : 0.f;
-      const int jr = e / kGT, dc = e % kGT;
-      Vs[jr][dc] = (j0 + jr < p.NB && d0 + dc < p.D) ? V[size_t(j0 + jr) * p.D + d0 + dc] : 0.f;
+  const int pr = threadIdx.x >> 2, pc = (threadIdx.x & 3) * 8;  // P loader: row, first of 8 columns
+  float acc[4][kCW] = {};
+  for (int j0 = 0; j0 < p.NB; j0 += kOJ) {
+    {
+      const int i = i0 + pr;
+      const float m = sm[pr], il = sl[pr];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int j = j0 + pc + e;
+        Ps[pc + e][pr] = (i < p.NB && j < p.NB) ? fast_exp2(fmaf(S[size_t(i) * p.NB + j], kLog2e, -m)) * il : 0.f;
+      }
+    }
+    for (int e = threadIdx.x; e < kOJ * D / 4; e += 256) {
+      const int jr = e / (D / 4), dc = (e % (D / 4)) * 4;
+      const float4 v = (j0 + jr < p.NB) ? *reinterpret_cast<const float4*>(V + size_t(j0 + jr) * D + dc)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(&Vs[jr][dc]) = v;
     }
     __syncthreads();
+#pragma unroll 8
+    for (int c = 0; c < kOJ; ++c) {
+      const float4 a = *reinterpret_cast<const float4*>(&Ps[c][ty * 4]);
+      float b[kCW];
 #pragma unroll
-    for (int c = 0; c < kGK; ++c) {
-      float a[4], b[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) { a[u] = Ps[c][ty * 4 + u]; b[u] = Vs[c][tx * 4 + u]; }
+      for (int g = 0; g < kCW / 4; ++g) {
+        const float4 v = *reinterpret_cast<const float4*>(&Vs[c][g * 64 + tx * 4]);
+        b[4 * g] = v.x; b[4 * g + 1] = v.y; b[4 * g + 2] = v.z; b[4 * g + 3] = v.w;
+      }
+      const float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
       for (int u = 0; u < 4; ++u)
 #pragma unroll
-        for (int w = 0; w < 4; ++w) acc[u][w] = fmaf(a[u], b[w], acc[u][w]);
+        for (int w = 0; w < kCW; ++w) acc[u][w] = fmaf(av[u], b[w], acc[u][w]);
     }
     __syncthreads();
   }
-  float* O = p.outc + size_t(bh) * p.NB * p.D;
+  float* O = p.outc + size_t(bh) * p.NB * D;
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
     const int i = i0 + ty * 4 + u;
     if (i >= p.NB) continue;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const int d = d0 + tx * 4 + w;
-      if (d < p.D) O[size_t(i) * p.D + d] = acc[u][w];
+    for (int g = 0; g < kCW / 4; ++g) {
+      const int d = g * 64 + tx * 4;
+      *reinterpret_cast<float4*>(O + size_t(i) * D + d) =
+          make_float4(acc[u][4 * g], acc[u][4 * g + 1], acc[u][4 * g + 2], acc[u][4 * g + 3]);
     }
   }
 }
@@ -222,8 +261,10 @@ cudaError_t launch_compressed_attention(const SelectParams& p, cudaStream_t stre
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  dim3 g3((p.D + kGT - 1) / kGT, (p.NB + kGT - 1) / kGT, BH);
-  outc_kernel<<<g3, 256, 0, stream>>>(p);
+  dim3 g3((p.NB + kOR - 1) / kOR, BH);
+  if (p.D == 128) outc_kernel<128><<<g3, 256, 0, stream>>>(p);
+  else if (p.D == 64) outc_kernel<64><<<g3, 256, 0, stream>>>(p);
+  else return cudaErrorInvalidValue;
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
