@@ -73,9 +73,14 @@ def attention_flops(p, n_sparse):
 # clocks during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = "uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
-             "clocks_event_reasons.sw_power_cap"
+    """SM clock and clock-event reasons of this rank's GPU, read through NVML
+    every 5 ms in a background thread (read-only queries; nothing is set), so
+    that even a timed region of a few tens of milliseconds is sampled.  Falls
+    back to `nvidia-smi -lms 100` when NVML is not importable."""
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
     def __init__(self, device):
         self.uuid = None
@@ -83,25 +88,59 @@ class ClockSampler:
             self.uuid = str(torch.cuda.get_device_properties(device).uuid)
         except Exception:  # noqa: BLE001
             pass
-        self.rows, self.proc, self.thread = [], None, None
+        self.rows, self.proc, self.thread, self.stop_flag, self.nvml = [], None, None, False, None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            import pynvml
+            pynvml.nvmlInit()
+            uid = self.uuid if self.uuid.startswith("GPU-") else "GPU-" + self.uuid
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(uid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.masks = [(n, getattr(pynvml, c)) for n, c in self.REASONS]
+            self.nvml = pynvml
+        except Exception:  # noqa: BLE001
+            self.nvml = None
+        if self.nvml is not None:
+            self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+            self.thread.start()
+            return
+        try:
+            fields = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                      "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                      "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:  # noqa: BLE001
             self.proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread = threading.Thread(target=self._read_smi, daemon=True)
         self.thread.start()
 
-    def _read(self):
+    def _poll_nvml(self):
+        nv = self.nvml
+        while not self.stop_flag:
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.rows.append((float(mhz), float(self.max_mhz), [n for n, m in self.masks if bits & m]))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.005)
+
+    def _read_smi(self):
+        names = [n for n, _ in self.REASONS]
         for line in self.proc.stdout:
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
+            if len(parts) >= 9 and (not self.uuid or self.uuid.replace("GPU-", "") in parts[0]):
+                try:
+                    self.rows.append((float(parts[1]), float(parts[2]),
+                                      [n for n, v in zip(names, parts[5:9]) if v.lower().startswith("active")]))
+                except ValueError:
+                    pass
 
     def stop(self):
+        self.stop_flag = True
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -111,17 +150,11 @@ class ClockSampler:
         if self.thread is not None:
             self.thread.join(timeout=5)
         rows = self.rows
-        if self.uuid:
-            mine = [r for r in rows if self.uuid.replace("GPU-", "") in r[0]]
-            rows = mine or rows
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, val in zip(names, r[5:9]) if val.lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted({n for r in rows for n in r[2]}), "samples": len(rows),
+                "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------
