@@ -61,17 +61,24 @@ ICSA_DEV float ex2(float x) {
   return y;
 }
 
-// Max / sum over 128 registers with 8 independent chains (a single chain
-// would serialise 128 dependent instructions).
+// Three-input maximum (sm_100 max.f32 with three sources).
+ICSA_DEV float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Max over 128 registers: 8 independent chains of three-input maxima (a single
+// chain would serialise the instructions).
 ICSA_DEV float max128(const float (&s)[128]) {
   float m[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) m[i] = s[i];
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(s[i], s[i + 8]);
 #pragma unroll
-  for (int c = 8; c < 128; ++c) m[c & 7] = fmaxf(m[c & 7], s[c]);
+  for (int c = 16; c < 128; c += 16)
 #pragma unroll
-  for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[i], m[i + 4]);
-  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+    for (int i = 0; i < 8; ++i) m[i] = fmax3(m[i], s[c + i], s[c + 8 + i]);
+  return fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
 }
 ICSA_DEV void tmem_load_row128(uint32_t taddr, float (&s)[128]) {
   uint32_t r[4][32];

@@ -211,12 +211,12 @@ ICSA_DEV void sparse_mma(const AttnParams& p, const STile& t, SSmem<D>& sm, uint
 ICSA_DEV float max64(const float (&s)[64]) {
   float m[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) m[i] = s[i];
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(s[i], s[i + 8]);
 #pragma unroll
-  for (int c = 8; c < 64; ++c) m[c & 7] = fmaxf(m[c & 7], s[c]);
+  for (int c = 16; c < 64; c += 16)
 #pragma unroll
-  for (int i = 0; i < 4; ++i) m[i] = fmaxf(m[i], m[i + 4]);
-  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+    for (int i = 0; i < 8; ++i) m[i] = fmax3(m[i], s[c + i], s[c + 8 + i]);
+  return fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
 }
 
 // The four softmax warps meet at named barrier 1 (staged masks and
