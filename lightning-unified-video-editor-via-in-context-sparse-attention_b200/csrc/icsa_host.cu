@@ -10,6 +10,10 @@
 //   caller's stream  icsa_forward on the group (H = group_heads)
 //   copy-out stream  D2H of the group's output columns
 //
+// The copy to the device is the slowest stream, so what remains after it is
+// the computation and copy back of the last group; the last full group is
+// therefore split into smaller groups (5 -> 3, 1, 1) to shorten that tail.
+//
 // A group of heads is a strided slice of the [B, S, H, D] host buffers: rows
 // of group_heads * D elements, H * D elements apart.  cudaMemcpy2DAsync copies
 // it to / from a compact [B, S, group_heads, D] device buffer.  Three buffer
@@ -21,6 +25,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "icsa_kernels.cuh"
 
@@ -154,13 +159,36 @@ ICSA_API int icsa_forward_host(const icsa_problem* p, int group_heads, const voi
   if ((e = cudaStreamWaitEvent(d->out, d->entry, 0)) != cudaSuccess) return host_cuda_fail(e, "stream wait");
 
   const size_t rows = size_t(p->B) * size_t(p->S);
-  const size_t cols = size_t(group_heads) * size_t(p->D);  // elements per row of a group
   const void* src[3] = {q, k, v};
   const int dts[3] = {p->q_dtype, p->k_dtype, p->v_dtype};
   const size_t eo = elem_size(p->out_dtype);
 
-  for (int g = 0; g < pl.groups; ++g) {
+  // group schedule: full groups, then the last full group in halving pieces
+  // (every piece is at most group_heads, the size the slots are laid out for)
+  std::vector<int> starts, sizes;
+  {
+    int h = 0;
+    for (int g = 0; g + 1 < pl.groups; ++g, h += group_heads) {
+      starts.push_back(h);
+      sizes.push_back(group_heads);
+    }
+    for (int rest = p->H - h; rest > 0;) {
+      const int piece = rest > 1 ? (rest + 1) / 2 : 1;
+      starts.push_back(h);
+      sizes.push_back(piece);
+      h += piece;
+      rest -= piece;
+    }
+  }
+  const int ng = int(sizes.size());
+
+  for (int g = 0; g < ng; ++g) {
     const int s = g % kSlots;
+    const int hg = sizes[g];
+    icsa_problem pg = pl.g;
+    pg.H = hg;
+    const size_t ws_g = icsa_workspace_size(&pg);
+    if (ws_g == 0 || ws_g > pl.ws_bytes) return host_fail(ICSA_ERR_INVALID, "group workspace");
     uint8_t* slot = base + 256 + size_t(s) * pl.slot_bytes;
     uint8_t* dev_in[3];
     size_t off = 0;
@@ -171,7 +199,8 @@ ICSA_API int icsa_forward_host(const icsa_problem* p, int group_heads, const voi
     uint8_t* dev_out = slot + off;
     off += align256(pl.out_bytes);
     uint8_t* ws = slot + off;
-    const size_t h0 = size_t(g) * size_t(group_heads);
+    const size_t h0 = size_t(starts[g]);
+    const size_t cols = size_t(hg) * size_t(p->D);  // elements per row of this group
 
     // copy in (after the copy-out of the group this slot held before)
     if (g >= kSlots && (e = cudaStreamWaitEvent(d->in, d->out_done[s], 0)) != cudaSuccess)
@@ -190,7 +219,7 @@ ICSA_API int icsa_forward_host(const icsa_problem* p, int group_heads, const voi
     if (p->alpha_mode == ICSA_ALPHA_TENSOR && alpha != nullptr)
       alpha_g = static_cast<const uint8_t*>(alpha) +
                 size_t(p->alpha_strides[2]) * h0 * elem_size(p->alpha_dtype);
-    rc = icsa_forward(&pl.g, dev_in[0], dev_in[1], dev_in[2], alpha_g, dev_out, ws, pl.ws_bytes, stream);
+    rc = icsa_forward(&pg, dev_in[0], dev_in[1], dev_in[2], alpha_g, dev_out, ws, ws_g, stream);
     if (rc != ICSA_OK) return rc;
     status_fold_kernel<<<1, 1, 0, stream>>>(status, reinterpret_cast<const int*>(ws));
     if ((e = cudaGetLastError()) != cudaSuccess) return host_cuda_fail(e, "status fold");
@@ -204,7 +233,7 @@ ICSA_API int icsa_forward_host(const icsa_problem* p, int group_heads, const voi
     if ((e = cudaEventRecord(d->out_done[s], d->out)) != cudaSuccess) return host_cuda_fail(e, "event record");
   }
   // the caller's stream completes when every output column is in host memory
-  for (int s = 0; s < kSlots && s < pl.groups; ++s)
+  for (int s = 0; s < kSlots && s < ng; ++s)
     if ((e = cudaStreamWaitEvent(stream, d->out_done[s], 0)) != cudaSuccess) return host_cuda_fail(e, "stream wait");
   return ICSA_OK;
 }
