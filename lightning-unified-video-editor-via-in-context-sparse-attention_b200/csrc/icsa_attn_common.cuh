@@ -99,13 +99,12 @@ ICSA_DEV float load_alpha(const AttnParams& p, int b, int token, int h, int d) {
 }
 
 
-// Residual epilogue for 32 consecutive features [d0, d0+32) of one output
-// row: x = bf16(o) + out_c * alpha, with the reference's dtype rounding
-// (attention outputs are bf16; out_compress and out_compress*alpha are bf16
-// when the reference computes them in bf16), stored as the output dtype.
-ICSA_DEV void store_out32(const AttnParams& p, int b, int token, int h, const float* oc_row, int d0,
-                          const float (&o)[32], size_t out_row) {
-  float x[32];
+// Residual for 32 consecutive features [d0, d0+32) of one output row:
+// x = bf16(o) + out_c * alpha, with the reference's dtype rounding (attention
+// outputs are bf16; out_compress and out_compress*alpha are bf16 when the
+// reference computes them in bf16).
+ICSA_DEV void residual32(const AttnParams& p, int b, int token, int h, const float* oc_row, int d0,
+                         const float (&o)[32], float (&x)[32]) {
 #pragma unroll
   for (int e = 0; e < 32; ++e) {
     const int d = d0 + e;
@@ -116,6 +115,13 @@ ICSA_DEV void store_out32(const AttnParams& p, int b, int token, int h, const fl
     if (p.ca_bf16) ca = bf16_round(ca);
     x[e] = bf16_round(o[e]) + ca;
   }
+}
+
+// The same, stored to the output row as the output dtype.
+ICSA_DEV void store_out32(const AttnParams& p, int b, int token, int h, const float* oc_row, int d0,
+                          const float (&o)[32], size_t out_row) {
+  float x[32];
+  residual32(p, b, token, h, oc_row, d0, o, x);
   if (p.out_dtype == ICSA_BF16) {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + out_row + d0;
 #pragma unroll

@@ -287,6 +287,11 @@ int run_attend(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, 
   a.alpha_scalar = p->alpha_scalar; a.alpha = alpha;
   for (int i = 0; i < 4; ++i) a.alpha_strides[i] = p->alpha_strides[i];
   a.out = out; a.out_dtype = p->out_dtype;
+  // bf16 output from a 16-byte aligned pointer: written by TMA stores
+  if (p->out_dtype == ICSA_BF16 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+    if ((rc = encode_rows_map(&maps.o, out, p->B, p->S, p->H, p->D)) != ICSA_OK) return rc;
+    a.out_tma = 1;
+  }
   a.err = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + L.err);
   if (parts & kAttendDense) {
     cudaError_t e = icsa::launch_flat_attention(a, maps, p->D, stream);

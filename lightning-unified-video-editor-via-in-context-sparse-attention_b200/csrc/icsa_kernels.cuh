@@ -89,6 +89,7 @@ struct AttnParams {
   // output [B, S, H, D]
   void* out;
   int out_dtype;
+  int out_tma;                   // 1: bf16 output written by TMA stores through maps.o
   int* err;
 };
 
@@ -98,6 +99,7 @@ struct AttnMaps {
   CUtensorMap v;
   CUtensorMap kc;  // bf16 [BH, nkv_pad, D] box {64, 128, 1}
   CUtensorMap vc;
+  CUtensorMap o;   // bf16 output [B, S, H, D] box {64, 1, 64, 1} (when out_tma)
 };
 
 // Block-sparse tiles (and, when flat_tiles > 0, single-tile dense tiles).

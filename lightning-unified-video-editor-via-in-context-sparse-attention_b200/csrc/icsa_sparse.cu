@@ -224,7 +224,7 @@ ICSA_DEV float max64(const float (&s)[64]) {
 // is set, later waits return at once, the loop runs on over stale data and
 // the error code marks the result invalid.
 template <int D>
-ICSA_DEV void sparse_softmax(const AttnParams& p, const STile& t, SSmem<D>& sm, uint32_t tmem) {
+ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const STile& t, SSmem<D>& sm, uint32_t tmem) {
   volatile int* abort_flag = &sm.abort_flag;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -320,40 +320,55 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const STile& t, SSmem<D>& sm, 
         asm volatile("bar.sync 1, 128;" ::: "memory");
         staged = true;
       }
-      // interval step: two BN=64 chunks of pooled blocks, all 128 columns
+      // interval step: two BN=64 chunks of pooled blocks, all 128 columns.
+      // Logits are q.KC / 64; dividing by 64 is exact, so the maxima are
+      // taken on the raw scores and 1/64 is folded into the exponent's
+      // multiplier.  Both chunks are masked and reduced first, then both
+      // exponentiated (chunk 1 uses the maximum after chunk 0, as the
+      // reference updates it chunk by chunk).
       float s[128];
       tmem_load_row128(s_col, s);
       const int ci = j - t.n_exact;
+      float cmax[2];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int chunk = 2 * ci + hh;
+        const int lim = p.nkv - chunk * 64;  // columns >= lim are beyond the extended KV
         const uint32_t w0 = mask_row[2 * chunk], w1 = mask_row[2 * chunk + 1];
         float cm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           const uint32_t w = c < 32 ? w0 : w1;
-          const bool valid = chunk * 64 + c < p.nkv && !((w >> (c & 31)) & 1u);
-          const float x = valid ? s[hh * 64 + c] * (1.0f / 64.0f) : -INFINITY;
+          const bool valid = c < lim && !((w >> (c & 31)) & 1u);
+          const float x = valid ? s[hh * 64 + c] : -INFINITY;
           s[hh * 64 + c] = x;
           cm[c & 3] = fmaxf(cm[c & 3], x);
         }
-        m_true = fmaxf(m_true, fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3])));
-        const float neg = -m_true * sl2;
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        cmax[hh] = fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3])) * (1.0f / 64.0f);
+      }
+      const float m0 = fmaxf(m_true, cmax[0]);
+      const float m1 = fmaxf(m0, cmax[1]);
+      m_true = m1;
+      const float sl2b = sl2 * (1.0f / 64.0f);
+      const float neg[2] = {-m0 * sl2, -m1 * sl2};
+      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-        for (int c = 0; c < 64; c += 4) {
+      for (int c = 0; c < 64; c += 4) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
           float* x = s + hh * 64 + c;
-          ffma2(x[0], x[1], x[0], x[1], sl2, sl2, neg, neg);
-          ffma2(x[2], x[3], x[2], x[3], sl2, sl2, neg, neg);
+          ffma2(x[0], x[1], x[0], x[1], sl2b, sl2b, neg[hh], neg[hh]);
+          ffma2(x[2], x[3], x[2], x[3], sl2b, sl2b, neg[hh], neg[hh]);
           x[0] = ex2(x[0]);
           x[1] = ex2(x[1]);
           x[2] = ex2(x[2]);
           x[3] = ex2(x[3]);
-          fadd2(a0, a1, a0, a1, x[0], x[1]);
-          fadd2(a2, a3, a2, a3, x[2], x[3]);
+          fadd2(acc[hh][0], acc[hh][1], acc[hh][0], acc[hh][1], x[0], x[1]);
+          fadd2(acc[hh][2], acc[hh][3], acc[hh][2], acc[hh][3], x[2], x[3]);
         }
-        g_l += ((a0 + a1) + (a2 + a3)) * 64.0f;
       }
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) g_l += ((acc[hh][0] + acc[hh][1]) + (acc[hh][2] + acc[hh][3])) * 64.0f;
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         uint32_t pk[32];
@@ -379,6 +394,55 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const STile& t, SSmem<D>& sm, 
   const bool write = (half == 0 || t.write1) && token < p.S;
   const float* oc = sm.outc[half];
   const size_t out_row = ((size_t(t.b) * p.S + token) * p.H + t.h) * D;
+  if (p.out_tma) {
+    // bf16 output: stage the 128 x D tile in the (now idle) first key stage in
+    // the TMA box layout (64 d per 128-byte row, 16-byte units swizzled with
+    // the row, block B 8 KB after block A), then one thread writes it with
+    // TMA stores (rows beyond S are clipped by the tensor map).
+    uint8_t* stage = sm.k[0];
+    const bool valid_row = token < p.S;
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t ro[32], rg[32];
+      __syncwarp();
+      tc::tmem_ld32(tmem + lanes + kSColO + c * 32, ro);
+      tc::tmem_ld32(tmem + lanes + kSColG + c * 32, rg);
+      tc::tmem_wait_ld();
+      float o[32], x[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) o[e] = fmaf(__uint_as_float(ro[e]), f, __uint_as_float(rg[e])) * inv;
+      if (valid_row) residual32(p, t.b, token, t.h, oc, c * 32, o, x);
+      else
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[e] = 0.f;
+      uint8_t* row = stage + (c >> 1) * kChunkBytes + tid * 128;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const uint32_t unit = uint32_t((c & 1) * 4 + v);
+        uint4 u;
+        u.x = pack_bf16x2(x[v * 8 + 0], x[v * 8 + 1]);
+        u.y = pack_bf16x2(x[v * 8 + 2], x[v * 8 + 3]);
+        u.z = pack_bf16x2(x[v * 8 + 4], x[v * 8 + 5]);
+        u.w = pack_bf16x2(x[v * 8 + 6], x[v * 8 + 7]);
+        *reinterpret_cast<uint4*>(row + ((unit ^ uint32_t(tid & 7)) << 4)) = u;
+      }
+    }
+    fence_proxy_async_smem();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (tid == 0) {
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb) {
+        if (hb == 1 && !t.write1) continue;
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_store_4d(&maps.o, stage + c * kChunkBytes + hb * (kChunkBytes / 2), c * 64, t.h, t.blk[hb] * kBlock,
+                       t.b);
+      }
+      bulk_commit();
+      bulk_wait_all();
+    }
+    return;
+  }
 #pragma unroll 1
   for (int c = 0; c < D / 32; ++c) {
     uint32_t ro[32], rg[32];
@@ -435,7 +499,7 @@ __global__ void __launch_bounds__(kSThreads, 1) sparse_kernel(const AttnParams p
   tc::fence_after_sync();
   const uint32_t tmem = sm.tmem_base;
   if (warp < 4) {
-    sparse_softmax<D>(p, t, sm, tmem);
+    sparse_softmax<D>(p, maps, t, sm, tmem);
   } else if (warp == kSProducerWarp) {
     if (lane == 0) {
       sparse_producer<D>(p, maps, t, sm);
