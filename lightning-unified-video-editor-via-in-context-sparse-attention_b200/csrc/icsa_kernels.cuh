@@ -102,8 +102,6 @@ struct AttnMaps {
   CUtensorMap o;   // bf16 output [B, S, H, D] box {64, 1, 64, 1} (when out_tma)
 };
 
-// Block-sparse tiles (and, when flat_tiles > 0, single-tile dense tiles).
-cudaError_t launch_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
 // Dense tiles of the flat query blocks, two 128-row tiles per CTA.
 cudaError_t launch_flat_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
 // Dense tiles of the flat query blocks for D = 128 on SM pairs (cta_group::2).
