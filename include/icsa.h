@@ -210,6 +210,16 @@ ICSA_API int icsa_forward_host(const icsa_problem* p, int group_heads, const voi
 ICSA_API int icsa_device_status(void* workspace, cudaStream_t stream);
 
 /*
+ * Self-test of the device-side bounded waits (no counterpart in the
+ * reference): launches a kernel whose mbarrier wait can never complete; the
+ * wait gives up after about one second, records a status code in the first
+ * word of `workspace` and returns, after which icsa_device_status(workspace)
+ * reports ICSA_ERR_DEVICE_TIMEOUT and the context stays usable.  Needs at
+ * least 256 bytes of device workspace.
+ */
+ICSA_API int icsa_wait_selftest(void* workspace, cudaStream_t stream);
+
+/*
  * Allocation-free variant of icsa_forward.  This entry point has no
  * counterpart in the reference; it exists for callers that cannot allocate
  * device memory where they make the call (a plugin host that owns all

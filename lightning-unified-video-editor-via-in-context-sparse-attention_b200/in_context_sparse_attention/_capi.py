@@ -20,7 +20,7 @@ STATUS = {0: "ICSA_OK", 1: "ICSA_ERR_INVALID", 2: "ICSA_ERR_UNSUPPORTED", 3: "IC
 
 EXPORTED = ("icsa_last_error", "icsa_version", "icsa_problem_init", "icsa_workspace_size",
             "icsa_get_workspace_layout", "icsa_forward", "icsa_pool", "icsa_select", "icsa_attend",
-            "icsa_attend_dense", "icsa_attend_sparse", "icsa_host_workspace_size", "icsa_forward_host",
+            "icsa_attend_dense", "icsa_attend_sparse", "icsa_host_workspace_size", "icsa_forward_host", "icsa_wait_selftest",
             "icsa_device_status")
 
 
@@ -98,6 +98,8 @@ def load(path: str = None) -> ctypes.CDLL:
         lib.icsa_host_workspace_size.restype = sz
         lib.icsa_forward_host.argtypes = [pp, i, vp, vp, vp, vp, vp, vp, sz, vp]
         lib.icsa_forward_host.restype = i
+        lib.icsa_wait_selftest.argtypes = [vp, vp]
+        lib.icsa_wait_selftest.restype = i
         lib.icsa_device_status.argtypes = [vp, vp]
         lib.icsa_device_status.restype = i
         _lib = lib

@@ -221,3 +221,26 @@ def test_720p_shape_properties(cuda_device):
     assert torch.isfinite(out.float()).all()
     again, _ = run_gpu(q, k, v, w.t_seq_len)
     assert torch.equal(out, again)
+
+
+def test_bounded_wait_reports_timeout_and_context_survives(cuda_device):
+    """A device wait that can never complete (an mbarrier nobody arrives at)
+    gives up after about a second: the status word reports the timeout to the
+    host, and the next call on the same context works."""
+    import time
+    from in_context_sparse_attention import _capi
+    lib = _capi.load()
+    ws = torch.zeros(256, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    t0 = time.time()
+    assert lib.icsa_wait_selftest(ws.data_ptr(), st) == 0
+    rc = lib.icsa_device_status(ws.data_ptr(), st)
+    waited = time.time() - t0
+    assert rc == 5, lib.icsa_last_error()
+    assert b"timeout" in lib.icsa_last_error().lower() or b"gave up" in lib.icsa_last_error().lower()
+    assert 0.5 < waited < 30.0
+    B, S, H, D, t = 1, 4096, 2, 128, 2048
+    q, k, v = (x.cuda() for x in _rand(B, S, H, D, torch.bfloat16, seed=5, t=t))
+    out, dbg = run_gpu(q, k, v, t)
+    assert torch.isfinite(out.float()).all()
+    assert lib.icsa_device_status(dbg["workspace"].data_ptr(), st) == 0
