@@ -117,6 +117,20 @@ ICSA_DEV void residual32(const AttnParams& p, int b, int token, int h, const flo
   }
 }
 
+// out_c * alpha for a scalar alpha, with the same rounding as residual32; it
+// is the same for every row of a query block, so kernels compute it once per
+// block (row of D values) and then use residual32_ca.
+ICSA_DEV float ca_scalar(const AttnParams& p, float cval) {
+  if (p.outc_bf16) cval = bf16_round(cval);
+  float ca = cval * p.alpha_scalar;
+  if (p.ca_bf16) ca = bf16_round(ca);
+  return ca;
+}
+ICSA_DEV void residual32_ca(const float* ca_row, int d0, const float (&o)[32], float (&x)[32]) {
+#pragma unroll
+  for (int e = 0; e < 32; ++e) x[e] = bf16_round(o[e]) + ca_row[d0 + e];
+}
+
 // The same, stored to the output row as the output dtype.
 ICSA_DEV void store_out32(const AttnParams& p, int b, int token, int h, const float* oc_row, int d0,
                           const float (&o)[32], size_t out_row) {

@@ -187,6 +187,10 @@ ICSA_DEV void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int 
 ICSA_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Waits until every committed bulk store of this thread has completed.
 ICSA_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Waits until every committed bulk store of this thread has read its shared
+// memory source (the global writes complete asynchronously), which is what a
+// CTA needs before it releases that shared memory.
+ICSA_DEV void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 ICSA_DEV void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

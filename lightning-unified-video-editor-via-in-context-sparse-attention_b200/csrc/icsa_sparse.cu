@@ -242,7 +242,10 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
     const int rk = hb ? t.rank[1] : t.rank[0];
     const int bk = hb ? t.blk[1] : t.blk[0];
     const float* oc_src = p.outc + (size_t(t.bh) * p.NB + bk) * D;
-    for (int d = i; d < D; d += 64) sm.outc[hb][d] = oc_src[d];
+    // scalar alpha: the residual term out_c * alpha of the block, rounded as the
+    // reference rounds it; tensor alpha: out_c itself (alpha varies by token)
+    const bool scalar = p.alpha_mode == ICSA_ALPHA_SCALAR;
+    for (int d = i; d < D; d += 64) sm.outc[hb][d] = scalar ? ca_scalar(p, oc_src[d]) : oc_src[d];
     if (mask_in_smem) {
       const uint32_t* msrc = p.sel_mask + (size_t(t.bh) * p.n_sparse + rk) * words;
       for (int w = i; w < words; w += 64) sm.mask[hb][w] = msrc[w];
@@ -392,7 +395,7 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
   const int blk = half ? t.blk[1] : t.blk[0];
   const int token = blk * kBlock + (tid & 63);
   const bool write = (half == 0 || t.write1) && token < p.S;
-  const float* oc = sm.outc[half];
+  const float* oc = sm.outc[half];  // out_c * alpha (scalar alpha) or out_c
   const size_t out_row = ((size_t(t.b) * p.S + token) * p.H + t.h) * D;
   if (p.out_tma) {
     // bf16 output: stage the 128 x D tile in the (now idle) first key stage in
@@ -401,7 +404,7 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
     // TMA stores (rows beyond S are clipped by the tensor map).
     uint8_t* stage = sm.k[0];
     const bool valid_row = token < p.S;
-#pragma unroll 1
+#pragma unroll 2
     for (int c = 0; c < D / 32; ++c) {
       uint32_t ro[32], rg[32];
       __syncwarp();
@@ -411,7 +414,8 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
       float o[32], x[32];
 #pragma unroll
       for (int e = 0; e < 32; ++e) o[e] = fmaf(__uint_as_float(ro[e]), f, __uint_as_float(rg[e])) * inv;
-      if (valid_row) residual32(p, t.b, token, t.h, oc, c * 32, o, x);
+      if (valid_row && p.alpha_mode == ICSA_ALPHA_SCALAR) residual32_ca(oc, c * 32, o, x);
+      else if (valid_row) residual32(p, t.b, token, t.h, oc, c * 32, o, x);
       else
 #pragma unroll
         for (int e = 0; e < 32; ++e) x[e] = 0.f;
@@ -439,7 +443,7 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
                        t.b);
       }
       bulk_commit();
-      bulk_wait_all();
+      bulk_wait_read();
     }
     return;
   }
@@ -455,7 +459,30 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
     for (int e = 0; e < 32; ++e) {
       o[e] = fmaf(__uint_as_float(ro[e]), f, __uint_as_float(rg[e])) * inv;
     }
-    if (write) store_out32(p, t.b, token, t.h, oc, c * 32, o, out_row);
+    if (!write) continue;
+    if (p.alpha_mode == ICSA_ALPHA_SCALAR) {
+      float x[32];
+      residual32_ca(oc, c * 32, o, x);
+      float* dst = reinterpret_cast<float*>(p.out) + out_row + c * 32;
+      if (p.out_dtype == ICSA_BF16) {
+        __nv_bfloat16* db = reinterpret_cast<__nv_bfloat16*>(p.out) + out_row + c * 32;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 u;
+          u.x = pack_bf16x2(x[v * 8 + 0], x[v * 8 + 1]);
+          u.y = pack_bf16x2(x[v * 8 + 2], x[v * 8 + 3]);
+          u.z = pack_bf16x2(x[v * 8 + 4], x[v * 8 + 5]);
+          u.w = pack_bf16x2(x[v * 8 + 6], x[v * 8 + 7]);
+          reinterpret_cast<uint4*>(db)[v] = u;
+        }
+      } else {
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          reinterpret_cast<float4*>(dst)[v] = make_float4(x[v * 4], x[v * 4 + 1], x[v * 4 + 2], x[v * 4 + 3]);
+      }
+    } else {
+      store_out32(p, t.b, token, t.h, oc, c * 32, o, out_row);
+    }
   }
 }
 
