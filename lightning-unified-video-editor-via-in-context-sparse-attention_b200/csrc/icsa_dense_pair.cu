@@ -48,6 +48,7 @@ struct __align__(1024) PSmem {
   uint8_t q[kPQBytes];
   uint8_t kv[kPStages][kPKBytes + kPVBytes];  // [K half | V half]
   float mref[2][128];  // [warpgroup][row] m_ref after that warpgroup's latest step
+  float ocs[2][128];   // per query block: out_c * alpha (scalar alpha) or out_c
   float lsum[2][128];  // epilogue: partial row sums and their origins
   float lmax[2][128];
   uint64_t q_full;
@@ -206,7 +207,7 @@ ICSA_DEV void pair_mma(const AttnParams& p, const PTile& t, PSmem& sm, uint32_t 
 // after a failed wait the abort flag is set, every later wait returns at
 // once, the loop runs on over stale data, and the error code marks the
 // result invalid.
-ICSA_DEV void pair_softmax(const AttnParams& p, const PTile& t, PSmem& sm, uint32_t tmem) {
+ICSA_DEV void pair_softmax(const AttnParams& p, const AttnMaps& maps, const PTile& t, PSmem& sm, uint32_t tmem) {
   volatile int* abort_flag = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int w = warp >> 2;                 // this warpgroup's step parity
@@ -218,6 +219,13 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const PTile& t, PSmem& sm, uint3
   const uint32_t s_base = tmem + lanes + kTmS;
   const uint32_t p_base = tmem + lanes + kTmP + 64u * uint32_t(w);  // + 128 for odd own steps
   const uint32_t o_base = tmem + lanes + kTmO;
+  // the residual term of the epilogue, one value per thread: block row >> 6,
+  // feature (row & 63) + 64 w (read after the epilogue's barrier 14)
+  {
+    const int hb = row >> 6, d = (row & 63) + 64 * w;
+    const float cval = p.outc[(size_t(t.bh) * p.NB + (hb ? t.blk[1] : t.blk[0])) * 128 + d];
+    sm.ocs[hb][d] = (p.alpha_mode == ICSA_ALPHA_SCALAR) ? ca_scalar(p, cval) : cval;
+  }
   const uint32_t s_free = pair::mapa(&sm.s_free[w], 0);
   const uint32_t p_full = pair::mapa(&sm.p_full[w], 0);
   const float sl2 = p.scale_log2;
@@ -324,12 +332,63 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const PTile& t, PSmem& sm, uint3
     if (mi != -INFINITY) lt += (mi == m_fin) ? li : li * ex2((mi - m_fin) * sl2);
   }
   const float inv = lt == 0.f ? 0.f : 1.0f / lt;
-  const int blk = (row < 64) ? t.blk[0] : t.blk[1];
-  const int wr = (row < 64) ? t.write[0] : t.write[1];
+  const int hb = row >> 6;
+  const int blk = hb ? t.blk[1] : t.blk[0];  // (no dynamic indexing: keeps the tile in registers)
   const int token = blk * kBlock + (row & 63);
-  const bool write = wr && token < p.S;
-  const float* oc = p.outc + (size_t(t.bh) * p.NB + blk) * 128;
+  const bool valid_row = token < p.S;
+  const bool write = (hb ? t.write[1] : t.write[0]) && valid_row;
+  pair::named_sync(14, 256);  // sm.ocs complete
+  const float* oc = sm.ocs[hb];
+  const bool scalar = p.alpha_mode == ICSA_ALPHA_SCALAR;
   const size_t out_row = ((size_t(t.b) * p.S + token) * p.H + t.h) * 128;
+  if (p.out_tma) {
+    // bf16 output: stage this CTA's 128 x 128 tile in the idle first K/V stage
+    // in the TMA box layout (64 d per 128-byte row, 16-byte units swizzled
+    // with the row, block B 8 KB after block A; warpgroup w fills d chunk w),
+    // then one thread writes it with TMA stores (rows beyond S are clipped).
+    uint8_t* stage = sm.kv[0];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      uint32_t r[32];
+      __syncwarp();
+      tc::tmem_ld32(o_base + 64u * uint32_t(w) + 32u * uint32_t(c), r);
+      tc::tmem_wait_ld();
+      float o[32], x[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(r[e]) * inv;
+      if (valid_row && scalar) residual32_ca(oc, 64 * w + 32 * c, o, x);
+      else if (valid_row) residual32(p, t.b, token, t.h, oc, 64 * w + 32 * c, o, x);
+      else
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[e] = 0.f;
+      uint8_t* rp = stage + w * kChunkBytes + row * 128;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const uint32_t unit = uint32_t(c * 4 + v);
+        uint4 u;
+        u.x = pack_bf16x2(x[v * 8 + 0], x[v * 8 + 1]);
+        u.y = pack_bf16x2(x[v * 8 + 2], x[v * 8 + 3]);
+        u.z = pack_bf16x2(x[v * 8 + 4], x[v * 8 + 5]);
+        u.w = pack_bf16x2(x[v * 8 + 6], x[v * 8 + 7]);
+        *reinterpret_cast<uint4*>(rp + ((unit ^ uint32_t(row & 7)) << 4)) = u;
+      }
+    }
+    fence_proxy_async_smem();
+    pair::named_sync(15, 256);
+    if (threadIdx.x == 0) {
+#pragma unroll
+      for (int b2 = 0; b2 < 2; ++b2) {
+        if (!t.write[b2]) continue;
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          tma_store_4d(&maps.o, stage + c * kChunkBytes + b2 * (kChunkBytes / 2), c * 64, t.h, t.blk[b2] * kBlock,
+                       t.b);
+      }
+      bulk_commit();
+      bulk_wait_read();
+    }
+    return;
+  }
 #pragma unroll 1
   for (int c = 0; c < 2; ++c) {
     uint32_t r[32];
@@ -339,7 +398,30 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const PTile& t, PSmem& sm, uint3
     float o[32];
 #pragma unroll
     for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(r[e]) * inv;
-    if (write) store_out32(p, t.b, token, t.h, oc, 64 * w + 32 * c, o, out_row);
+    if (!write) continue;
+    if (scalar) {
+      float x[32];
+      residual32_ca(oc, 64 * w + 32 * c, o, x);
+      if (p.out_dtype == ICSA_BF16) {
+        __nv_bfloat16* db = reinterpret_cast<__nv_bfloat16*>(p.out) + out_row + 64 * w + 32 * c;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 u;
+          u.x = pack_bf16x2(x[v * 8 + 0], x[v * 8 + 1]);
+          u.y = pack_bf16x2(x[v * 8 + 2], x[v * 8 + 3]);
+          u.z = pack_bf16x2(x[v * 8 + 4], x[v * 8 + 5]);
+          u.w = pack_bf16x2(x[v * 8 + 6], x[v * 8 + 7]);
+          reinterpret_cast<uint4*>(db)[v] = u;
+        }
+      } else {
+        float* df = reinterpret_cast<float*>(p.out) + out_row + 64 * w + 32 * c;
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          reinterpret_cast<float4*>(df)[v] = make_float4(x[v * 4], x[v * 4 + 1], x[v * 4 + 2], x[v * 4 + 3]);
+      }
+    } else {
+      store_out32(p, t.b, token, t.h, oc, 64 * w + 32 * c, o, out_row);
+    }
   }
 }
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
@@ -387,7 +469,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   // a warpgroup.
   if (warp < 8) {
     tc::reg_alloc<216>();
-    pair_softmax(p, t, sm, tmem);
+    pair_softmax(p, maps, t, sm, tmem);
   } else {
     tc::reg_dealloc<72>();
   }
