@@ -57,3 +57,11 @@ def test_result_dtypes_follow_torch_promotion(dts, alpha):
     q = torch.zeros(1, 8, 1, 4, dtype=dts[0])
     outc = torch.zeros(1, 8, 1, 4, dtype=want[0])
     assert (q + outc * alpha).dtype == want[2]
+
+
+def test_default_head_groups_divide_and_stay_small():
+    """Head groups for host streaming: a divisor of H, about eight groups,
+    at least four heads per group when H allows."""
+    for H, want in ((40, 5), (20, 4), (10, 2), (5, 1), (64, 8), (2, 2), (3, 3), (7, 1)):
+        g = esa_mod._default_group_heads(H)
+        assert H % g == 0 and g == want, (H, g)
