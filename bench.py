@@ -1,7 +1,7 @@
 """Benchmark of the in-context sparse attention call (BASELINE metric:
 "sparse-attn ms/call at 65K joint tokens (40h x 128d bf16) 1/2/4/8 GPU").
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload 480p|720p|config1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload 480p|720p|config1|dit-step]
                     [--impl b200|reference]
 
 One step is one whole call over all 40 heads.  With N GPUs (torchrun, one
@@ -23,6 +23,12 @@ maximum over ranks: total work per call is fixed, so scaling is "strong".
 * cpu_baseline / --impl reference: the CPU restatement of the reference path
   (the reference's PyTorch orchestration + restated kernels) on the host
   cores: the whole call for one or two heads, scaled to all 40 heads.
+
+--workload dit-step measures the other half of the metric, "DiT step s": one
+denoising step of a random-init Wan 2.2 A14B-shaped DiT (40 blocks, CFG pair
+as batch 2) on the 480p joint sequence, Ulysses sequence-parallel over the
+ranks (wan_dit); its line reports seconds per step and the whole step's
+tensor throughput.
 """
 from __future__ import annotations
 
@@ -247,6 +253,11 @@ def run_reference_arm(args, rank):
     the host cores (rank 0 only)."""
     if rank != 0:
         return
+    if args.workload == "dit-step":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference's DiT step runs its attention in "
+                          "GPU-only TileLang/flash-attn kernels, and a CPU restatement of a 40-block A14B step "
+                          "is hours of host time"}), flush=True)
+        return
     w = WORKLOADS[args.workload]
     for _ in range(args.warmup):
         cpu_reference_sample(w)
@@ -265,6 +276,125 @@ def run_reference_arm(args, rank):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# DiT step: one denoising step of the A14B-shaped DiT
+# ---------------------------------------------------------------------------
+DIT_LATENT = (16, 21, 60, 104)   # 480p latent (VAE stride 4x8x8): 21 x 30 x 52 = 32760 patches per video
+DIT_SEQ = 65536                  # joint tokens: 32760 target | 32760 source | 16 padding
+DIT_LAUNCHES_PER_BLOCK = 9 + 13  # 3 LayerNorm, 3 RMSNorm/RoPE, 3 residual passes + one unaligned attention call
+
+
+def dit_step_flops(cfg, B, S, t_seq_len):
+    """Algorithmic FLOPs of one step (2 FLOP per MAC): the block GEMMs, the
+    cross-attention, the sparse self-attention and the embeddings/head."""
+    C, Fd, L, H, D = cfg.dim, cfg.ffn_dim, cfg.text_len, cfg.num_heads, cfg.head_dim
+    T = B * S
+    gemm = 2.0 * T * C * (3 * C + 1) + 2.0 * T * C * C          # q, k, v, alpha_1; o
+    gemm += 2.0 * 2 * T * C * C + 2.0 * B * L * C * 2 * C        # cross q, o; cross k | v
+    gemm += 2.0 * 2 * T * C * Fd                                 # FFN
+    cross = 4.0 * B * S * L * C
+    attn = attention_flops(_capi.problem(B, S, H, D, t_seq_len), _capi.workspace_layout(
+        _capi.problem(B, S, H, D, t_seq_len)).n_sparse)[0]
+    per_block = gemm + cross + attn
+    outer = 2.0 * S * 64 * C + 2.0 * B * L * (cfg.text_dim * C + C * C) + 2.0 * T * C * 64
+    return cfg.num_layers * per_block + outer, cfg.num_layers * attn
+
+
+def run_dit_step(args, world, rank, local):
+    """Seconds per denoising step of the Wan 2.2 A14B-shaped DiT (40 layers,
+    dim 5120, 40 heads, FFN 13824; CFG pair as batch 2; 512 text tokens) on
+    the 480p joint 65,536-token sequence, with Ulysses sequence parallelism
+    over the ranks.  Random-init weights, synthetic latents and text."""
+    import datetime
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from wan_dit import WanDiT, WanDiTConfig
+    cfg = WanDiTConfig(num_layers=args.dit_layers)
+    model = WanDiT(cfg, device=dev, seed=0)
+    g = torch.Generator().manual_seed(0)
+    latent = torch.randn(*DIT_LATENT, generator=g)
+    source = 0.8 * latent + 0.6 * torch.randn(*DIT_LATENT, generator=g)
+    context = torch.randn(2, cfg.text_len, cfg.text_dim, generator=g)
+    hl, hs, hc = (x.pin_memory() for x in (latent, source, context))
+    dl, ds, dc = (x.to(dev) for x in (latent, source, context))
+    hout = torch.empty(DIT_LATENT).pin_memory()
+    t_seq_len = DIT_LATENT[1] * (DIT_LATENT[2] // 2) * (DIT_LATENT[3] // 2)
+
+    def step(l_, s_, c_):
+        return model.denoise_step(l_, s_, 999.0, 1.0, 31.0 / 32.0, c_, DIT_SEQ)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(dl, ds, dc)
+    barrier()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        out = step(dl, ds, dc)
+    e1.record()
+    barrier()
+    clk = clocks.stop()
+    sec = e0.elapsed_time(e1) / 1e3 / args.steps
+    del out
+
+    # e2e: latents and text from pinned host memory in, the updated latent out
+    e2e_sec = None
+    if not args.no_e2e:
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        f0.record()
+        for _ in range(args.steps):
+            nl = step(hl.to(dev, non_blocking=True), hs.to(dev, non_blocking=True), hc.to(dev, non_blocking=True))
+            hout.copy_(nl, non_blocking=True)
+        f1.record()
+        barrier()
+        e2e_sec = f0.elapsed_time(f1) / 1e3 / args.steps
+    if dist is not None:
+        t = torch.tensor([sec, e2e_sec or 0.0], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sec, e2e_sec = float(t[0]), (float(t[1]) if e2e_sec is not None else None)
+    flops, attn_flops = dit_step_flops(cfg, 2, DIT_SEQ, t_seq_len)
+    sustained, burst, _, src = peaks()
+    achieved = flops / sec / 1e12 / world
+    if rank == 0:
+        line = {"metric": METRIC, "value": sec, "unit": "s/step", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": False, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, N(0,1) latents and text)",
+                "config": {"workload": "wan22_a14b_dit_step_480p_cfg2", "layers": cfg.num_layers, "dim": cfg.dim,
+                           "heads": cfg.num_heads, "ffn": cfg.ffn_dim, "text_tokens": cfg.text_len, "cfg_batch": 2,
+                           "seq_len": DIT_SEQ, "t_seq_len": t_seq_len, "latent": list(DIT_LATENT),
+                           "parallelism": f"ulysses x{world}",
+                           "l2": "every step streams 28 GB of weights; no flush"},
+                "roofline": {"bound": "tensor", "kernel": "whole step (cuBLAS GEMMs + this library's kernels)",
+                             "achieved": achieved, "peak": sustained, "unit": "TFLOP/s per GPU",
+                             "frac": achieved / sustained, "peak_kind": f"{src} sustained bf16",
+                             "flops_per_step": flops, "attention_flops_per_step": attn_flops, "traffic": None},
+                "clocks": clk, "gpu_launches": (DIT_LAUNCHES_PER_BLOCK * cfg.num_layers + 1) * args.steps,
+                "cpu_baseline": None}
+        if e2e_sec is not None:
+            line["e2e"] = {"value": e2e_sec, "unit": "s/step", "path": "WanDiT.denoise_step on pinned host latents",
+                           "h2d_bytes_per_step": (hl.numel() + hs.numel() + hc.numel()) * 4,
+                           "d2h_bytes_per_step": hout.numel() * 4}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def config_dict(w, n):
     return {"workload": w.name, "B": w.B, "H": w.H, "D": w.D, "S": w.S, "t_seq_len": w.t_seq_len,
             "grid": list(w.grid), "heads_per_gpu": w.H // n, "parallelism": f"head-sharded x{n}",
@@ -277,7 +407,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="480p", choices=list(WORKLOADS))
+    ap.add_argument("--workload", default="480p", choices=list(WORKLOADS) + ["dit-step"])
+    ap.add_argument("--dit-layers", type=int, default=40, help="blocks of the DiT step (40 is the A14B model)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -290,6 +421,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference_arm(args, rank)
+        return
+    if args.workload == "dit-step":
+        run_dit_step(args, world, rank, local)
         return
 
     import datetime

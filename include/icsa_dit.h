@@ -1,0 +1,113 @@
+/*
+ * icsa_dit.h -- C ABI of the fused elementwise stages of one Wan 2.2 DiT
+ * block (libicsa.so), the code that surrounds the in-context sparse
+ * attention call in the reference's model (model.py:128-288).
+ *
+ * The GEMMs of the block (q/k/v/o projections, cross-attention projections,
+ * FFN) are plain library GEMMs and stay with the caller; these entry points
+ * are the memory-bound passes between them, each one HBM pass:
+ *
+ *   icsa_dit_modulated_norm  LayerNorm, then `* scale + shift`, written as
+ *                            the bf16 operand of the next GEMM
+ *                            (model.py:256 `norm1(x).float() * (1 + e[1]) + e[0]`,
+ *                             :263 `norm2(x).float() * (1 + e[4]) + e[3]`,
+ *                             :262 `norm3(x)` with its affine weight / bias,
+ *                             :288 the head's norm; WanLayerNorm :116-121)
+ *   icsa_dit_norm_rope       RMSNorm of q and k over the model width, the 3D
+ *                            rotary embedding in float64, v passed through,
+ *                            all written straight into the layout the
+ *                            attention (or the Ulysses all-to-all) reads, and
+ *                            the per-token gate alpha_1
+ *                            (model.py:152-170, rope_apply :69-95, WanRMSNorm :102-113)
+ *   icsa_dit_gated_residual  x += y * gate in float32
+ *                            (model.py:259 `x + y * e[2]`, :262 `x + cross_attn(..)`,
+ *                             :265 `x + y * e[5]`)
+ *
+ * Conventions as in icsa.h: plain device pointers, element counts and
+ * strides in elements, asynchronous on `stream`, an icsa_status return and
+ * icsa_last_error() for the message.  bf16 buffers must be 16-byte aligned
+ * and their leading dimensions multiples of 8 elements.
+ */
+#ifndef ICSA_DIT_H_
+#define ICSA_DIT_H_
+
+#include "icsa.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/*
+ * out[r, c] = bf16( n[r, c] * scale[b, c] + shift[b, c] ),  b = r / rows_per_batch,
+ * n = LayerNorm(x[r, :]) without affine terms (biased variance, eps inside the
+ * square root), rounded to bf16 first when `round_norm_bf16` is set (the
+ * reference's `type_as(x)` for a bf16 residual stream).  The product and the
+ * sum are rounded separately, as the reference's two float32 ops are.
+ *   x:     [rows, ldx] of x_dtype (ICSA_F32 or ICSA_BF16), C columns used
+ *   scale, shift: float32, row b at b * batch_stride (0 = one row for all)
+ *   out:   bf16 [rows, C], contiguous
+ * C must be a multiple of 8 and at most 8192.
+ */
+ICSA_API int icsa_dit_modulated_norm(const void* x, int x_dtype, int64_t ldx, int rows, int C, int rows_per_batch,
+                                     const float* scale, int64_t scale_batch_stride, const float* shift,
+                                     int64_t shift_batch_stride, float eps, int round_norm_bf16, void* out,
+                                     cudaStream_t stream);
+
+/*
+ * Up to three vectors of width C = heads * D per row, taken from bf16 rows of
+ * leading dimension `ld` (for a fused q|k|v GEMM output, src[j] = base + j*C).
+ * Vector j gets, when norm_weight[j] is non-NULL, the reference's WanRMSNorm:
+ *     bf16( bf16( x * rsqrt(mean(x^2) + eps) ) * weight )
+ * then, when rope[j] is set, the rotary embedding of rope_apply computed in
+ * float64: pair i of head h of token t is multiplied by (cos, sin) =
+ * rope_table[pos][i], pos being the token's frame, row or column index for
+ * pairs [0, split1), [split1, split2), [split2, D/2); tokens whose
+ * token_pos[t].rotate is 0 pass unrotated (the reference's padding with ones).
+ * The result is stored as dst_dtype[j] at element offset
+ *     b*dst_batch_stride + (h / heads_per_group)*dst_group_stride
+ *       + t_local*dst_token_stride + (h % heads_per_group)*D + d
+ * so that [B, S, H, D] (one group) and the per-destination blocks of an
+ * all-to-all are both plain layouts.
+ * The optional gate reads column `gate_src` of every row (bf16, same ld) and
+ * writes the reference's alpha_1 = (sigmoid(a) - 0.5) * 0.5 with each op
+ * rounded to bf16 (model.py:162), to gate_dst[r] (bf16 [rows]).
+ */
+typedef struct icsa_dit_norm_rope_desc {
+  int rows, C, D;
+  int64_t ld;
+  int rows_per_batch;       /* tokens of one batch element in this call (t_local < rows_per_batch) */
+  int token_offset;         /* global token index of t_local = 0                         */
+  float eps;
+  int count;                /* vectors per row, 1..3                                     */
+  const void* src[3];
+  const void* norm_weight[3];
+  int rope[3];
+  void* dst[3];
+  int dst_dtype[3];
+  int heads_per_group;
+  int64_t dst_batch_stride, dst_group_stride, dst_token_stride;
+  const double* rope_table; /* [rope_positions][D/2][2] (cos, sin)                       */
+  int rope_positions;
+  const int* token_pos;     /* [global tokens][4]: frame, row, column, rotate             */
+  int token_count;          /* entries of token_pos                                      */
+  int rope_split1, rope_split2;
+  const void* gate_src;     /* NULL: no gate                                              */
+  void* gate_dst;
+} icsa_dit_norm_rope_desc;
+
+ICSA_API int icsa_dit_norm_rope(const icsa_dit_norm_rope_desc* desc, cudaStream_t stream);
+
+/*
+ * x[r, c] = x[r, c] + y[r, c] * gate[b, c]  in float32 (product and sum
+ * rounded separately), b = r / rows_per_batch; gate NULL means x + y.
+ *   x: float32 [rows, C] contiguous;  y: bf16 [rows, ldy];  gate: float32,
+ *   row b at b * gate_batch_stride.
+ */
+ICSA_API int icsa_dit_gated_residual(float* x, const void* y, int64_t ldy, int rows, int C, int rows_per_batch,
+                                     const float* gate, int64_t gate_batch_stride, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ICSA_DIT_H_ */

@@ -1,0 +1,199 @@
+"""Operations of one Wan 2.2 DiT block, as the model in this package calls them.
+
+`CudaOps` is the implementation: the fused elementwise passes and the
+in-context sparse attention run in libicsa.so (include/icsa_dit.h,
+include/icsa.h); the projections are library GEMMs (torch.nn.functional.linear,
+i.e. cuBLAS, bf16 in / bf16 out with f32 accumulation, which is what the
+reference's nn.Linear computes under CUDA autocast); the cross-attention over
+the 512 text tokens is torch's scaled_dot_product_attention, the library
+counterpart of the reference's flash_attention call (wanx/attention.py:18-85).
+Constructing it loads libicsa.so and raises if it is missing: there is no CPU
+fallback.
+
+Every method takes and returns torch tensors on the current CUDA device and
+runs on the current stream.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.nn.functional as F
+
+from in_context_sparse_attention import _capi
+
+DIT_EXPORTED = ("icsa_dit_modulated_norm", "icsa_dit_norm_rope", "icsa_dit_gated_residual")
+
+_DT = {torch.bfloat16: _capi.ICSA_BF16, torch.float32: _capi.ICSA_F32}
+
+
+class NormRopeDesc(ctypes.Structure):
+    """Mirror of struct icsa_dit_norm_rope_desc."""
+    _fields_ = [
+        ("rows", ctypes.c_int), ("C", ctypes.c_int), ("D", ctypes.c_int),
+        ("ld", ctypes.c_int64),
+        ("rows_per_batch", ctypes.c_int), ("token_offset", ctypes.c_int),
+        ("eps", ctypes.c_float),
+        ("count", ctypes.c_int),
+        ("src", ctypes.c_void_p * 3), ("norm_weight", ctypes.c_void_p * 3), ("rope", ctypes.c_int * 3),
+        ("dst", ctypes.c_void_p * 3), ("dst_dtype", ctypes.c_int * 3),
+        ("heads_per_group", ctypes.c_int),
+        ("dst_batch_stride", ctypes.c_int64), ("dst_group_stride", ctypes.c_int64),
+        ("dst_token_stride", ctypes.c_int64),
+        ("rope_table", ctypes.c_void_p), ("rope_positions", ctypes.c_int),
+        ("token_pos", ctypes.c_void_p), ("token_count", ctypes.c_int),
+        ("rope_split1", ctypes.c_int), ("rope_split2", ctypes.c_int),
+        ("gate_src", ctypes.c_void_p), ("gate_dst", ctypes.c_void_p),
+    ]
+
+
+def _load():
+    lib = _capi.load()
+    for name in DIT_EXPORTED:
+        if not hasattr(lib, name):
+            raise ImportError(f"{_capi.LIB_PATH} does not export {name}; rebuild it with `python build.py`")
+    vp, i, i64, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+    lib.icsa_dit_modulated_norm.argtypes = [vp, i, i64, i, i, i, vp, i64, vp, i64, f, i, vp, vp]
+    lib.icsa_dit_modulated_norm.restype = i
+    lib.icsa_dit_norm_rope.argtypes = [ctypes.POINTER(NormRopeDesc), vp]
+    lib.icsa_dit_norm_rope.restype = i
+    lib.icsa_dit_gated_residual.argtypes = [vp, vp, i64, i, i, i, vp, i64, vp]
+    lib.icsa_dit_gated_residual.restype = i
+    return lib
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _rows(x: torch.Tensor):
+    """(rows, leading dimension) of a 2-D row-major view."""
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError(f"expected a 2-D row-major view, got shape {tuple(x.shape)} strides {x.stride()}")
+    return x.shape[0], x.stride(0)
+
+
+class CudaOps:
+    """The B200 implementation of the block's operations."""
+
+    def __init__(self):
+        self.lib = _load()
+
+    # --- library GEMMs and activations -----------------------------------
+    @staticmethod
+    def linear(x, w, b=None):
+        return F.linear(x, w, b)
+
+    @staticmethod
+    def gelu_tanh(x):
+        return F.gelu(x, approximate="tanh")
+
+    # --- fused elementwise passes ----------------------------------------
+    def modulated_norm(self, x, scale, shift, rows_per_batch, eps, round_norm=False):
+        """bf16 [rows, C] = LayerNorm(x) * scale[b] + shift[b] (include/icsa_dit.h).
+        scale / shift: f32 [B, C] or [C] (shared by all rows)."""
+        rows, ld = _rows(x)
+        C = x.shape[1]
+        nb = -(-rows // rows_per_batch)
+        for t in (scale, shift):
+            if t.dtype != torch.float32 or t.shape[-1] != C or t.stride(-1) != 1 or (t.dim() == 2 and t.shape[0] < nb):
+                raise ValueError(f"modulated_norm: scale/shift must be f32 [{nb}, {C}] or [{C}]")
+        out = torch.empty(rows, C, dtype=torch.bfloat16, device=x.device)
+        sbs = scale.stride(0) if scale.dim() == 2 else 0
+        hbs = shift.stride(0) if shift.dim() == 2 else 0
+        _capi.check(self.lib.icsa_dit_modulated_norm(
+            x.data_ptr(), _DT[x.dtype], ld, rows, C, rows_per_batch, scale.data_ptr(), sbs, shift.data_ptr(), hbs,
+            float(eps), int(bool(round_norm)), out.data_ptr(), _stream()), "icsa_dit_modulated_norm")
+        return out
+
+    def norm_rope(self, jobs, rows_per_batch, eps, token_offset=0, table=None, token_pos=None, splits=(0, 0),
+                  gate=None):
+        """jobs: up to three (src [rows, C] bf16 view, norm weight or None,
+        rope flag, out [B, G, s, hp, D] contiguous).  gate: optional
+        (src [rows] bf16 column view, out bf16 [rows])."""
+        d = NormRopeDesc()
+        src0 = jobs[0][0]
+        rows, ld = _rows(src0)
+        out0 = jobs[0][3]
+        B, G, s, hp, D = out0.shape
+        if s != rows_per_batch or rows != B * s or G * hp * D != src0.shape[1]:
+            raise ValueError(f"norm_rope: output layout {tuple(out0.shape)} does not hold {rows} rows of "
+                             f"{src0.shape[1]} values in batches of {rows_per_batch}")
+        if table is not None and (token_pos.shape[1] != 4 or token_pos.dtype != torch.int32
+                                  or token_offset + s > token_pos.shape[0] or not token_pos.is_contiguous()):
+            raise ValueError("norm_rope: token_pos must be contiguous int32 [tokens, 4] covering this shard")
+        if table is not None and (table.dtype != torch.float64 or table.shape[1:] != (D // 2, 2)
+                                  or not table.is_contiguous()):
+            raise ValueError(f"norm_rope: the rotary table must be contiguous f64 [positions, {D // 2}, 2]")
+        if gate is not None and (gate[1].numel() < rows or gate[1].dtype != torch.bfloat16):
+            raise ValueError(f"norm_rope: the gate output must be bf16 with {rows} entries")
+        d.rows, d.C, d.D, d.ld = rows, src0.shape[1], D, ld
+        d.rows_per_batch, d.token_offset, d.eps, d.count = rows_per_batch, token_offset, float(eps), len(jobs)
+        for j, (src, w, rope, out) in enumerate(jobs):
+            if _rows(src) != (rows, ld) or out.shape != out0.shape or not out.is_contiguous():
+                raise ValueError("norm_rope: all vectors must share rows, leading dimension and output layout")
+            d.src[j] = src.data_ptr()
+            d.norm_weight[j] = w.data_ptr() if w is not None else None
+            d.rope[j] = int(bool(rope))
+            d.dst[j] = out.data_ptr()
+            d.dst_dtype[j] = _DT[out.dtype]
+        d.heads_per_group = hp
+        d.dst_batch_stride, d.dst_group_stride, d.dst_token_stride = out0.stride(0), out0.stride(1), out0.stride(2)
+        if table is not None:
+            d.rope_table, d.rope_positions = table.data_ptr(), table.shape[0]
+            d.token_pos, d.token_count = token_pos.data_ptr(), token_pos.shape[0]
+            d.rope_split1, d.rope_split2 = splits
+        if gate is not None:
+            gsrc, gout = gate
+            if gsrc.stride(0) != ld:
+                raise ValueError("norm_rope: the gate column must share the rows' leading dimension")
+            d.gate_src, d.gate_dst = gsrc.data_ptr(), gout.data_ptr()
+        _capi.check(self.lib.icsa_dit_norm_rope(ctypes.byref(d), _stream()), "icsa_dit_norm_rope")
+
+    def gated_residual_(self, x, y, gate, rows_per_batch):
+        """x (f32 [rows, C], in place) += y (bf16 [rows, C] view) * gate[b] (f32 [B, C] or None)."""
+        if x.dtype != torch.float32 or not x.is_contiguous():
+            raise ValueError("gated_residual_: x must be a contiguous f32 tensor")
+        rows, ldy = _rows(y)
+        C = x.shape[-1]
+        if x.shape != (rows, y.shape[1]):
+            raise ValueError(f"gated_residual_: x {tuple(x.shape)} and y {tuple(y.shape)} differ")
+        if gate is not None and (gate.dtype != torch.float32 or gate.shape[-1] != C or gate.stride(-1) != 1
+                                 or gate.shape[0] < -(-rows // rows_per_batch)):
+            raise ValueError("gated_residual_: gate must be f32 [batches, C]")
+        gp, gbs = (gate.data_ptr(), gate.stride(0)) if gate is not None else (None, 0)
+        _capi.check(self.lib.icsa_dit_gated_residual(x.data_ptr(), y.data_ptr(), ldy, rows, C, rows_per_batch, gp, gbs,
+                                                     _stream()), "icsa_dit_gated_residual")
+        return x
+
+    # --- attention ---------------------------------------------------------
+    def self_attention(self, q, k, v, alpha, t_seq_len):
+        """In-context sparse attention of the reference's WanSelfAttention
+        (model.py:172-173) for q, k f32 and v bf16 [B, S, h, D] and the bf16
+        gate alpha [B, S], returned as the bf16 operand of the output
+        projection (the reference's f32 result rounded once to bf16, which is
+        what its autocast o-projection reads)."""
+        B, S, H, D = q.shape
+        p = _capi.problem(B, S, H, D, int(t_seq_len))
+        p.q_dtype, p.k_dtype, p.v_dtype = _DT[q.dtype], _DT[k.dtype], _DT[v.dtype]
+        p.out_dtype = _capi.ICSA_BF16
+        p.outc_bf16, p.ca_bf16 = 1, 1
+        p.alpha_mode, p.alpha_dtype = _capi.ICSA_ALPHA_TENSOR, _DT[alpha.dtype]
+        for i, st in enumerate((alpha.stride(0), alpha.stride(1), 0, 0)):
+            p.alpha_strides[i] = st
+        lib = self.lib
+        size = lib.icsa_workspace_size(ctypes.byref(p))
+        if size == 0:
+            _capi.check(1, "icsa_workspace_size")
+        ws = torch.empty(size, dtype=torch.uint8, device=q.device)
+        out = torch.empty(B, S, H, D, dtype=torch.bfloat16, device=q.device)
+        _capi.check(lib.icsa_forward(ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), alpha.data_ptr(),
+                                     out.data_ptr(), ws.data_ptr(), size, _stream()), "icsa_forward")
+        return out
+
+    @staticmethod
+    def cross_attention(q, k, v):
+        """Softmax attention of bf16 q [B, L, H, D] over k, v [B, Lk, H, D]
+        with the default 1/sqrt(D) scale; bf16 [B, L, H, D]."""
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+        return o.transpose(1, 2)

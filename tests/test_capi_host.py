@@ -1,5 +1,5 @@
 """Host-side checks of the C ABI (CPU only, no kernel launches): the library
-loads, exports every function include/icsa.h declares, derives the
+loads, exports every function include/*.h declares, derives the
 reference's block counts, lays out its workspace consistently and rejects
 invalid problems with the documented status codes."""
 import ctypes
@@ -11,12 +11,16 @@ import pytest
 from in_context_sparse_attention import _capi
 from oracle import icsa_oracle as orc
 
-HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "icsa.h")
+INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
 
 
 def declared_functions():
-    text = open(HEADER).read()
-    return sorted(set(re.findall(r"ICSA_API\s+[\w\s\*]+?\b(icsa_\w+)\s*\(", text)))
+    names = set()
+    for h in sorted(os.listdir(INCLUDE)):
+        if h.endswith(".h"):
+            text = open(os.path.join(INCLUDE, h)).read()
+            names |= set(re.findall(r"ICSA_API\s+[\w\s\*]+?\b(icsa_\w+)\s*\(", text))
+    return sorted(names)
 
 
 def test_library_exports_every_declared_function():

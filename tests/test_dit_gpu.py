@@ -1,0 +1,188 @@
+"""GPU parity of the DiT harness's fused passes (libicsa.so, include/icsa_dit.h)
+and of whole blocks against the reference's block math restated in torch
+(tests/_dit_reference.py).
+
+Tolerances: the fused passes round exactly where the reference rounds, so
+they agree with the restatement except where a float32 row statistic
+(mean, variance, mean square) summed in a different order moves a value
+across a bf16 rounding boundary: such elements must stay within one bf16
+unit (or 1e-6 where `n * scale + shift` cancels) and be rare.  The gate and
+the residual update are elementwise with identical rounding and must agree
+bit for bit.  Whole steps (two tiny blocks; one full-width block) are bf16
+GEMM chains; they agree with the restated model within 1e-2 in mean-abs
+(relative to the output's mean magnitude), 2e-2 at the 99.9th percentile
+and 6e-2 at the maximum (relative to its largest value)."""
+import pytest
+import torch
+
+from _dit_reference import ReferenceOps
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(dim=256, ffn_dim=512, num_heads=2, num_layers=2, freq_dim=32, text_dim=64, text_len=16, in_dim=4,
+            out_dim=4)
+
+
+@pytest.fixture(scope="module")
+def ops(cuda_device):
+    from wan_dit._ops import CudaOps
+    return CudaOps()
+
+
+def bf16_ulps(a, b):
+    """Distance in units of the bf16 spacing at |b|."""
+    a, b = a.float(), b.float()
+    ulp = torch.ldexp(torch.ones_like(b), (torch.frexp(b.abs().clamp_min(1e-30))[1] - 8))
+    return (a - b).abs() / ulp
+
+
+def assert_step_close(got, ref):
+    """Whole-model outputs: bf16 GEMM chains plus the few selections that a
+    last-bit change of q or k can flip; judged on the mean and on the tail."""
+    err = (got - ref).abs().flatten().float()
+    rel_mean = float(err.mean() / ref.abs().mean())
+    rel_q999 = float(torch.quantile(err[:: max(1, err.numel() // 1000000)], 0.999) / ref.abs().max())
+    rel_max = float(err.max() / ref.abs().max())
+    assert rel_mean <= 1e-2 and rel_q999 <= 2e-2 and rel_max <= 6e-2, (rel_mean, rel_q999, rel_max)
+
+
+def assert_bf16_close(got, ref, max_ulps=1.0, max_frac=2e-3, atol=1e-6):
+    """At most one bf16 unit apart, or `atol` apart where `n * scale + shift`
+    cancels to a value much smaller than its terms (a float32 unit of the
+    terms is then many bf16 units of the result); differences rare."""
+    d = (got.float() - ref.float()).abs()
+    u = bf16_ulps(got, ref)
+    frac = float((d > 0).float().mean())
+    bad = (u > max_ulps) & (d > atol)
+    assert not bool(bad.any()) and frac <= max_frac, (float(u.max()), float(d.max()), frac)
+
+
+@pytest.mark.parametrize("C,rows,xdt,round_norm", [(5120, 1031, torch.float32, False),
+                                                    (5120, 512, torch.bfloat16, True),
+                                                    (256, 300, torch.float32, False),
+                                                    (6144, 64, torch.float32, False)])
+def test_modulated_norm_matches_reference_math(ops, C, rows, xdt, round_norm):
+    g = torch.Generator(device="cuda").manual_seed(C + rows)
+    B = 2 if rows % 2 == 0 else 1
+    x = (torch.randn(rows, C, generator=g, device="cuda") * 3 + 0.5).to(xdt)
+    scale = 1 + 0.1 * torch.randn(B, C, generator=g, device="cuda")
+    shift = 0.1 * torch.randn(B, C, generator=g, device="cuda")
+    got = ops.modulated_norm(x, scale, shift, rows // B, 1e-6, round_norm)
+    ref = ReferenceOps().modulated_norm(x, scale, shift, rows // B, 1e-6, round_norm)
+    assert got.dtype == torch.bfloat16 and got.shape == (rows, C)
+    atol = 1e-6
+    if round_norm:
+        # the normalised value is itself rounded to bf16 first: a flip there
+        # moves the result by one bf16 unit of n times the scale
+        n = torch.nn.functional.layer_norm(x.float(), (C,), eps=1e-6)
+        per_row = scale[torch.arange(rows, device="cuda") // (rows // B)]
+        atol = 1e-6 + 2.0 ** -6 * n.abs() * per_row.abs()
+    assert_bf16_close(got, ref, atol=atol)
+
+
+def test_affine_norm_shares_one_weight_row(ops):
+    C, rows = 5120, 256
+    x = torch.randn(rows, C, device="cuda")
+    w = 1 + 0.1 * torch.randn(C, device="cuda")
+    b = 0.1 * torch.randn(C, device="cuda")
+    got = ops.modulated_norm(x, w, b, 128, 1e-6)
+    ref = ReferenceOps().modulated_norm(x, w, b, 128, 1e-6)
+    assert_bf16_close(got, ref)
+
+
+@pytest.mark.parametrize("groups", [1, 2, 8])
+def test_norm_rope_matches_reference_math_and_layout(ops, groups):
+    from wan_dit import head_dim_splits, rope_table, token_positions
+    B, H, D = 2, 40, 128
+    C = H * D
+    grid = (3, 8, 10)                       # 240 tokens per video
+    S = 2 * 240 + 16
+    s = S // groups
+    rank = groups - 1                       # the last shard: source tokens and padding
+    g = torch.Generator(device="cuda").manual_seed(groups)
+    qkv = torch.randn(B * s, 3 * C + 8, generator=g, device="cuda").to(torch.bfloat16)
+    wq = (1 + 0.1 * torch.randn(C, generator=g, device="cuda")).to(torch.bfloat16)
+    wk = (1 + 0.1 * torch.randn(C, generator=g, device="cuda")).to(torch.bfloat16)
+    table = rope_table(D).cuda()
+    pos = token_positions(grid, grid, S).cuda()
+    hp = H // groups
+    outs = {}
+    for name, impl in (("got", ops), ("ref", ReferenceOps())):
+        q = torch.empty(B, groups, s, hp, D, device="cuda")
+        k = torch.empty_like(q)
+        v = torch.empty(B, groups, s, hp, D, dtype=torch.bfloat16, device="cuda")
+        gate = torch.empty(B * s, dtype=torch.bfloat16, device="cuda")
+        impl.norm_rope([(qkv[:, :C], wq, True, q), (qkv[:, C:2 * C], wk, True, k), (qkv[:, 2 * C:3 * C], None, False, v)],
+                       rows_per_batch=s, eps=1e-6, token_offset=rank * s, table=table, token_pos=pos,
+                       splits=head_dim_splits(D), gate=(qkv[:, 3 * C], gate))
+        outs[name] = (q, k, v, gate)
+    (q, k, v, gate), (rq, rk, rv, rgate) = outs["got"], outs["ref"]
+    assert torch.equal(v, rv) and torch.equal(gate, rgate)
+    for a, b in ((q, rq), (k, rk)):
+        d = (a - b).abs()
+        exact = float((d == 0).float().mean())
+        # rotated bf16 values: a bf16 flip of the RMSNorm output moves a pair by about one bf16 unit
+        assert exact >= 0.998 and float(d.max()) <= 2 ** -7 * float(b.abs().max()), (exact, float(d.max()))
+
+
+def test_gated_residual_is_bit_exact(ops):
+    rows, C, B = 512, 5120, 2
+    x = torch.randn(rows, C, device="cuda")
+    y = torch.randn(rows, 3 * C, device="cuda").to(torch.bfloat16)[:, C:2 * C]
+    gate = torch.randn(B, C, device="cuda")
+    a, b = x.clone(), x.clone()
+    ops.gated_residual_(a, y, gate, rows // B)
+    ReferenceOps().gated_residual_(b, y, gate, rows // B)
+    assert torch.equal(a, b)
+    ops.gated_residual_(a, y, None, rows // B)
+    ReferenceOps().gated_residual_(b, y, None, rows // B)
+    assert torch.equal(a, b)
+
+
+def test_invalid_arguments_raise(ops):
+    from in_context_sparse_attention._capi import IcsaError
+    x = torch.randn(4, 100, device="cuda")          # C not a multiple of 8
+    with pytest.raises(IcsaError):
+        ops.modulated_norm(x, torch.ones(100, device="cuda"), torch.zeros(100, device="cuda"), 4, 1e-6)
+
+
+def _tiny_inputs(cfg, grid=(4, 16, 34)):
+    g = torch.Generator().manual_seed(0)
+    latent = torch.randn(cfg.in_dim, *grid, generator=g)
+    source = 0.8 * latent + 0.6 * torch.randn(cfg.in_dim, *grid, generator=g)
+    context = torch.randn(2, cfg.text_len, cfg.text_dim, generator=g)
+    return latent.cuda(), source.cuda(), context.cuda()
+
+
+def test_tiny_dit_step_matches_reference_block_math(ops):
+    """Two blocks with the product path (fused passes + sparse attention
+    kernels) against the reference's math with the CPU oracle attention."""
+    from wan_dit import WanDiT, WanDiTConfig
+    cfg = WanDiTConfig(**TINY)
+    latent, source, context = _tiny_inputs(cfg)
+    seq_len = 2 * 4 * 8 * 17 + 32
+    got = WanDiT(cfg, seed=3, ops=ops).forward(latent, source, 500.0, context, seq_len)
+    ref = WanDiT(cfg, seed=3, ops=ReferenceOps()).forward(latent, source, 500.0, context, seq_len)
+    assert got.shape == ref.shape == (2, 4, 4, 16, 34)
+    assert_step_close(got, ref)
+
+
+def test_full_width_block_matches_reference_block_math(ops):
+    """One A14B-width block (C = 5120, 40 heads, FFN 13824) on a short
+    sequence: the fused passes at full width against the reference's math,
+    both using this package's attention so that only the elementwise chain
+    is compared."""
+    from wan_dit import WanDiT, WanDiTConfig
+    cfg = WanDiTConfig(num_layers=1)
+    grid = (2, 16, 32)                      # 256 tokens per video after 2x2 patches
+    g = torch.Generator().manual_seed(1)
+    latent = torch.randn(cfg.in_dim, 2, 32, 64, generator=g).cuda()
+    source = (0.8 * latent.cpu() + 0.6 * torch.randn(latent.shape, generator=g)).cuda()
+    context = torch.randn(2, cfg.text_len, cfg.text_dim, generator=g).cuda()
+    seq_len = 2 * 2 * 16 * 32 + 64
+    got = WanDiT(cfg, seed=5, ops=ops).forward(latent, source, 900.0, context, seq_len)
+    ref = WanDiT(cfg, seed=5, ops=ReferenceOps(attention=ops.self_attention)).forward(
+        latent, source, 900.0, context, seq_len)
+    assert got.shape == (2, cfg.out_dim, 2, 32, 64) and bool(torch.isfinite(got).all())
+    assert grid == (2, 16, 32)
+    assert_step_close(got, ref)

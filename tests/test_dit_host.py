@@ -1,0 +1,129 @@
+"""CPU checks of the Wan 2.2 DiT harness around the attention call
+(wan_dit): rotary tables against the reference's own formulas, token
+positions, and Ulysses sequence parallelism over two gloo ranks against one
+rank, with the block math restated in torch (tests/_dit_reference.py)."""
+import datetime
+import os
+import socket
+import sys
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(REPO, "lightning-unified-video-editor-via-in-context-sparse-attention_b200")
+
+from wan_dit import WanDiTConfig, head_dim_splits, rope_table, token_positions  # noqa: E402
+
+from _dit_reference import reference_freqs, rope_apply_tokens  # noqa: E402
+
+TINY = dict(dim=256, ffn_dim=512, num_heads=2, num_layers=2, freq_dim=32, text_dim=64, text_len=16, in_dim=4,
+            out_dim=4)
+
+
+def tiny_inputs(cfg, seed=0, grid=(4, 16, 34)):
+    g = torch.Generator().manual_seed(seed)
+    f, h, w = grid
+    latent = torch.randn(cfg.in_dim, f, h, w, generator=g)
+    source = 0.8 * latent + 0.6 * torch.randn(cfg.in_dim, f, h, w, generator=g)
+    context = torch.randn(2, cfg.text_len, cfg.text_dim, generator=g)
+    return latent, source, context
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_rope_table_equals_reference_frequencies(D):
+    ref = reference_freqs(D)
+    tab = rope_table(D)
+    assert tab.shape == (1024, D // 2, 2) and tab.dtype == torch.float64
+    assert torch.equal(tab[..., 0], ref.real) and torch.equal(tab[..., 1], ref.imag)
+
+
+def test_head_dim_splits_follow_the_reference():
+    assert head_dim_splits(128) == (22, 43)
+    assert head_dim_splits(64) == (12, 22)
+
+
+def test_token_positions_cover_target_source_and_padding():
+    pos = token_positions((2, 3, 4), (2, 3, 4), 64)
+    assert pos.shape == (64, 4) and pos.dtype == torch.int32
+    assert pos[:24, 3].all() and pos[24:48, 3].all() and not pos[48:, 3].any()
+    assert pos[0].tolist() == [0, 0, 0, 1] and pos[23].tolist() == [1, 2, 3, 1]
+    assert pos[24].tolist() == [0, 0, 0, 1] and pos[5].tolist() == [0, 1, 1, 1]
+    with pytest.raises(ValueError):
+        token_positions((2, 3, 4), (2, 3, 4), 40)
+
+
+def test_rope_restatement_rotates_pairs_and_skips_padding():
+    D = 128
+    pos = token_positions((1, 2, 2), (1, 2, 2), 10)
+    x = torch.randn(1, 10, 2, D)
+    y = rope_apply_tokens(x, pos, reference_freqs(D))
+    assert torch.equal(y[:, 8:], x[:, 8:])                       # padding: multiplied by ones
+    # rotation keeps the norm of every complex pair
+    nx = x[:, :8].reshape(1, 8, 2, D // 2, 2).norm(dim=-1)
+    ny = y[:, :8].reshape(1, 8, 2, D // 2, 2).norm(dim=-1)
+    assert torch.allclose(nx, ny, rtol=1e-5, atol=1e-6)
+
+
+def test_default_config_is_the_a14b_expert():
+    cfg = WanDiTConfig()
+    assert (cfg.dim, cfg.ffn_dim, cfg.num_heads, cfg.num_layers, cfg.head_dim) == (5120, 13824, 40, 40, 128)
+    assert (cfg.text_dim, cfg.text_len, cfg.freq_dim, cfg.patch_size) == (4096, 512, 256, (1, 2, 2))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker_ulysses_dit(rank, world, port, q):
+    try:
+        for p in (REPO, PKG, os.path.join(REPO, "tests")):
+            if p not in sys.path:
+                sys.path.insert(0, p)
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+        torch.set_num_threads(2)
+        from wan_dit import WanDiT, WanDiTConfig
+        from _dit_reference import ReferenceOps
+        cfg = WanDiTConfig(**TINY)
+        latent, source, context = tiny_inputs(cfg)
+        seq_len = 2 * 4 * 8 * 17 + 32          # 1120 tokens: target 544 | source 544 | 32 padding
+        solo = [dist.new_group([r]) for r in range(world)][rank]
+        sharded = WanDiT(cfg, device="cpu", seed=3, ops=ReferenceOps())
+        single = WanDiT(cfg, device="cpu", seed=3, ops=ReferenceOps(), group=solo)
+        assert sharded.world == world and single.world == 1
+        a = sharded.forward(latent, source, 500.0, context, seq_len)
+        b = single.forward(latent, source, 500.0, context, seq_len)
+        err = float((a - b).abs().max())
+        scale = float(b.abs().max())
+        q.put((rank, err, scale, tuple(a.shape), bool(torch.isfinite(a).all())))
+    except Exception as e:  # noqa: BLE001
+        import traceback
+        q.put((rank, repr(e) + traceback.format_exc(), None, None, None))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_ulysses_step_on_two_ranks_equals_one_rank():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_ulysses_dit, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, err, scale, shape, finite in results:
+        assert scale is not None, err
+        assert shape == (2, 4, 4, 16, 34) and finite
+        # the two runs differ only in GEMM row blocking (bf16 outputs) and the
+        # exchanges, which move bytes unchanged
+        assert err <= 2e-2 * scale, (rank, err, scale)
