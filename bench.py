@@ -280,7 +280,13 @@ def run_reference_arm(args, rank):
 # DiT step: one denoising step of the A14B-shaped DiT
 # ---------------------------------------------------------------------------
 DIT_LATENT = (16, 21, 60, 104)   # 480p latent (VAE stride 4x8x8): 21 x 30 x 52 = 32760 patches per video
-DIT_SEQ = 65536                  # joint tokens: 32760 target | 32760 source | 16 padding
+
+
+def dit_seq_len(latent):
+    """Joint tokens: target | source | padding to a multiple of 512 (65536 for
+    the 480p latent: 32760 | 32760 | 16), so that 8 ranks hold whole blocks."""
+    t = latent[1] * (latent[2] // 2) * (latent[3] // 2)
+    return -(-2 * t // 512) * 512
 DIT_LAUNCHES_PER_BLOCK = 9 + 13  # 3 LayerNorm, 3 RMSNorm/RoPE, 3 residual passes + one unaligned attention call
 
 
@@ -317,18 +323,20 @@ def run_dit_step(args, world, rank, local):
     torch.cuda.set_device(dev)
     from wan_dit import WanDiT, WanDiTConfig
     cfg = WanDiTConfig(num_layers=args.dit_layers)
-    model = WanDiT(cfg, device=dev, seed=0)
+    model = WanDiT(cfg, device=dev, seed=0, pipelined=not args.dit_no_pipeline)
     g = torch.Generator().manual_seed(0)
-    latent = torch.randn(*DIT_LATENT, generator=g)
-    source = 0.8 * latent + 0.6 * torch.randn(*DIT_LATENT, generator=g)
+    shape = (DIT_LATENT[0], args.dit_frames, DIT_LATENT[2], DIT_LATENT[3])
+    seq = dit_seq_len(shape)
+    latent = torch.randn(*shape, generator=g)
+    source = 0.8 * latent + 0.6 * torch.randn(*shape, generator=g)
     context = torch.randn(2, cfg.text_len, cfg.text_dim, generator=g)
     hl, hs, hc = (x.pin_memory() for x in (latent, source, context))
     dl, ds, dc = (x.to(dev) for x in (latent, source, context))
-    hout = torch.empty(DIT_LATENT).pin_memory()
-    t_seq_len = DIT_LATENT[1] * (DIT_LATENT[2] // 2) * (DIT_LATENT[3] // 2)
+    hout = torch.empty(shape).pin_memory()
+    t_seq_len = shape[1] * (shape[2] // 2) * (shape[3] // 2)
 
     def step(l_, s_, c_):
-        return model.denoise_step(l_, s_, 999.0, 1.0, 31.0 / 32.0, c_, DIT_SEQ)
+        return model.denoise_step(l_, s_, 999.0, 1.0, 31.0 / 32.0, c_, seq)
 
     def barrier():
         if dist is not None:
@@ -367,17 +375,21 @@ def run_dit_step(args, world, rank, local):
         t = torch.tensor([sec, e2e_sec or 0.0], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         sec, e2e_sec = float(t[0]), (float(t[1]) if e2e_sec is not None else None)
-    flops, attn_flops = dit_step_flops(cfg, 2, DIT_SEQ, t_seq_len)
+    flops, attn_flops = dit_step_flops(cfg, 2, seq, t_seq_len)
     sustained, burst, _, src = peaks()
     achieved = flops / sec / 1e12 / world
     if rank == 0:
         line = {"metric": METRIC, "value": sec, "unit": "s/step", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": False, "scaling": "strong",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, N(0,1) latents and text)",
-                "config": {"workload": "wan22_a14b_dit_step_480p_cfg2", "layers": cfg.num_layers, "dim": cfg.dim,
+                "config": {"workload": "wan22_a14b_dit_step_480p_cfg2" if args.dit_frames == DIT_LATENT[1] and
+                           cfg.num_layers == 40 else f"wan22_a14b_dit_step_f{args.dit_frames}_l{cfg.num_layers}",
+                           "layers": cfg.num_layers, "dim": cfg.dim,
                            "heads": cfg.num_heads, "ffn": cfg.ffn_dim, "text_tokens": cfg.text_len, "cfg_batch": 2,
-                           "seq_len": DIT_SEQ, "t_seq_len": t_seq_len, "latent": list(DIT_LATENT),
+                           "seq_len": seq, "t_seq_len": t_seq_len, "latent": list(shape),
                            "parallelism": f"ulysses x{world}",
+                           "exchange": "one all-to-all per tensor" if args.dit_no_pipeline or world == 1
+                           else "per batch element, overlapped with compute",
                            "l2": "every step streams 28 GB of weights; no flush"},
                 "roofline": {"bound": "tensor", "kernel": "whole step (cuBLAS GEMMs + this library's kernels)",
                              "achieved": achieved, "peak": sustained, "unit": "TFLOP/s per GPU",
@@ -409,6 +421,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="480p", choices=list(WORKLOADS) + ["dit-step"])
     ap.add_argument("--dit-layers", type=int, default=40, help="blocks of the DiT step (40 is the A14B model)")
+    ap.add_argument("--dit-no-pipeline", action="store_true", help="DiT step: unpipelined Ulysses exchanges")
+    ap.add_argument("--dit-frames", type=int, default=DIT_LATENT[1],
+                    help="latent frames of the DiT step (21 is 480p video; fewer give a small profiling case)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

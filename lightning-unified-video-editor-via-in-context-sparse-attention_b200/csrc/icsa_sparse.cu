@@ -385,8 +385,13 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
     mbar_arrive(&sm.p_full[j & 1]);
   }
 
-  // epilogue: (acc * f + g_acc) / (l * f + g_l), f re-bases acc and l on the final max
-  warp_mbar_wait(&sm.pv_done, uint32_t(n - 1) & 1u, p.err, kErrPvDone, abort_flag);
+  // epilogue: (acc * f + g_acc) / (l * f + g_l), f re-bases acc and l on the final max.
+  // Wait for every MMA of the tile on the single-phase mma_fin barrier.  A
+  // parity wait on pv_done cannot express "P.V(n-1) done" here: S(j+1) is
+  // issued before P.V(j), so s_full(n-1) only implies that P.V(n-3) is done;
+  // with P.V(n-2) still in flight pv_done sits two phases back and a wait
+  // for parity (n-1)&1 would see the older phase complete and return early.
+  warp_mbar_wait(&sm.mma_fin, 0u, p.err, kErrPvDone, abort_flag);
   tc::fence_after_sync();
   if (!staged) asm volatile("bar.sync 1, 128;" ::: "memory");
   const float f = ex2((m_ref - m_true) * sl2);

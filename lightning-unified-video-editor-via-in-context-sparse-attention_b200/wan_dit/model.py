@@ -104,13 +104,17 @@ class WanDiT:
     """Random-init Wan 2.2 DiT whose self-attention is the in-context sparse
     attention of this package.
 
-    ops:   the block operations (default: `_ops.CudaOps`, which needs
-           libicsa.so and a CUDA device).
-    group: process group of the Ulysses ranks (default: the default group
-           when torch.distributed is initialised, else a single rank).
+    ops:       the block operations (default: `_ops.CudaOps`, which needs
+               libicsa.so and a CUDA device).
+    group:     process group of the Ulysses ranks (default: the default group
+               when torch.distributed is initialised, else a single rank).
+    pipelined: with several ranks, overlap each batch element's exchanges
+               with the other's computation (`_self_attention_pipelined`);
+               False runs one exchange per tensor for the whole batch.
     """
 
-    def __init__(self, cfg: WanDiTConfig = WanDiTConfig(), device=None, seed: int = 0, ops=None, group=None):
+    def __init__(self, cfg: WanDiTConfig = WanDiTConfig(), device=None, seed: int = 0, ops=None, group=None,
+                 pipelined: bool = True):
         if ops is None:
             from ._ops import CudaOps
             ops = CudaOps()
@@ -118,6 +122,7 @@ class WanDiT:
         self.cfg = cfg
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.group = group
+        self.pipelined = pipelined
         self.dist = dist.is_available() and dist.is_initialized()
         self.world = dist.get_world_size(group) if self.dist else 1
         self.rank = dist.get_rank(group) if self.dist else 0
@@ -150,6 +155,7 @@ class WanDiT:
         self.rope_table = rope_mod.rope_table(D).to(self.device)
         self.rope_splits = rope_mod.head_dim_splits(D)
         self._pos_key = None
+        self._time_f32 = None
 
     # ------------------------------------------------------------------
     # embeddings
@@ -183,10 +189,13 @@ class WanDiT:
     def time_embed(self, t: torch.Tensor):
         """e [N, C] and e0 [N, 6, C] in f32 (model.py:434-437)."""
         lin = torch.nn.functional.linear
+        if self._time_f32 is None:   # f32 copies of the time MLP, made once (the reference runs it in f32)
+            self._time_f32 = [w.float() for w in (self.w_time1, self.b_time1, self.w_time2, self.b_time2,
+                                                  self.w_tproj, self.b_tproj)]
+        w1, b1, w2, b2, wp, bp = self._time_f32
         x = sinusoidal_embedding_1d(self.cfg.freq_dim, t).float()
-        e = lin(torch.nn.functional.silu(lin(x, self.w_time1.float(), self.b_time1.float())),
-                self.w_time2.float(), self.b_time2.float())
-        e0 = lin(torch.nn.functional.silu(e), self.w_tproj.float(), self.b_tproj.float())
+        e = lin(torch.nn.functional.silu(lin(x, w1, b1)), w2, b2)
+        e0 = lin(torch.nn.functional.silu(e), wp, bp)
         return e, e0.unflatten(1, (6, self.cfg.dim))
 
     def text_embed(self, context: torch.Tensor):
@@ -244,23 +253,19 @@ class WanDiT:
 
         # self-attention (model.py:255-259)
         xin = ops.modulated_norm(x, e["scale0"], e["shift0"], s, cfg.eps, round_norm=first)
-        qkv = ops.linear(xin, blk.w_qkv, blk.b_qkv)
         dev = x.device
-        q = torch.empty(B, n, s, hp, D, dtype=torch.float32, device=dev)
-        k = torch.empty_like(q)
-        v = torch.empty(B, n, s, hp, D, dtype=torch.bfloat16, device=dev)
-        gate = torch.empty(B * s, dtype=torch.bfloat16, device=dev)
-        ops.norm_rope([(qkv[:, :C], blk.norm_q, True, q), (qkv[:, C:2 * C], blk.norm_k, True, k),
-                       (qkv[:, 2 * C:3 * C], None, False, v)], rows_per_batch=s, eps=cfg.eps,
-                      token_offset=self.rank * s, table=self.rope_table, token_pos=self.token_pos,
-                      splits=self.rope_splits, gate=(qkv[:, 3 * C], gate))
-        del xin
-        qf, kf, vf, alpha = self._exchange_in(q, k, v, gate)
-        del qkv, q, k, v
-        o = ops.self_attention(qf, kf, vf, alpha, t_seq_len)
-        del qf, kf, vf
-        y = ops.linear(self._exchange_out(o), blk.w_o, blk.b_o)
-        del o
+        if n > 1 and self.pipelined:
+            y = self._self_attention_pipelined(blk, xin, B, s, t_seq_len)
+        else:
+            qkv = ops.linear(xin, blk.w_qkv, blk.b_qkv)
+            q, k, v, gate = self._qkv(blk, qkv, B, s)
+            del xin, qkv
+            qf, kf, vf, alpha = self._exchange_in(q, k, v, gate)
+            del q, k, v
+            o = ops.self_attention(qf, kf, vf, alpha, t_seq_len)
+            del qf, kf, vf
+            y = ops.linear(self._exchange_out(o), blk.w_o, blk.b_o)
+            del o
         if x.dtype != torch.float32:
             x = x.float()
         ops.gated_residual_(x, y, e["gate0"], s)
@@ -285,6 +290,69 @@ class WanDiT:
         del h
         ops.gated_residual_(x, y, e["gate1"], s)
         return x
+
+    def _qkv(self, blk: _Block, qkv, B, s):
+        """RMSNorm + RoPE of q and k, v passed through, all written into the
+        all-to-all send layout [B, world, s, H/world, D], and the gate alpha_1
+        (model.py:153-170), from the fused projection output qkv [B*s, 3C+8]."""
+        cfg = self.cfg
+        C, D, n = cfg.dim, cfg.head_dim, self.world
+        hp = cfg.num_heads // n
+        q = torch.empty(B, n, s, hp, D, dtype=torch.float32, device=qkv.device)
+        k = torch.empty_like(q)
+        v = torch.empty(B, n, s, hp, D, dtype=torch.bfloat16, device=qkv.device)
+        gate = torch.empty(B * s, dtype=torch.bfloat16, device=qkv.device)
+        self.ops.norm_rope([(qkv[:, :C], blk.norm_q, True, q), (qkv[:, C:2 * C], blk.norm_k, True, k),
+                            (qkv[:, 2 * C:3 * C], None, False, v)], rows_per_batch=s, eps=cfg.eps,
+                           token_offset=self.rank * s, table=self.rope_table, token_pos=self.token_pos,
+                           splits=self.rope_splits, gate=(qkv[:, 3 * C], gate))
+        return q, k, v, gate
+
+    def _self_attention_pipelined(self, blk: _Block, xin, B, s, t_seq_len):
+        """Ulysses self-attention with the exchanges of one batch element
+        overlapping the computation of the other: NCCL runs the all-to-alls on
+        its own stream, each launched as soon as its operand is written, and
+        the compute stream waits for an exchange only right before its result
+        is read:
+
+            projection+RoPE b0 | projection+RoPE b1 | attention b0 | attention b1 | o-proj b0 | o-proj b1
+                               | exchange-in b0     | exchange-in b1 | exchange-out b0 | exchange-out b1
+
+        Every rank issues the same collectives in the same order."""
+        ops, g = self.ops, self.group
+        cfg = self.cfg
+        C, D, n = cfg.dim, cfg.head_dim, self.world
+        hp = cfg.num_heads // n
+        S = n * s
+        inbound = []
+        for b in range(B):
+            qkv = ops.linear(xin[b * s:(b + 1) * s], blk.w_qkv, blk.b_qkv)
+            q, k, v, gate = self._qkv(blk, qkv, 1, s)
+            del qkv
+            qf = torch.empty(1, S, hp, D, dtype=torch.float32, device=xin.device)
+            kf = torch.empty_like(qf)
+            vf = torch.empty(1, S, hp, D, dtype=torch.bfloat16, device=xin.device)
+            alpha = torch.empty(1, S, dtype=torch.bfloat16, device=xin.device)
+            works = [dist.all_to_all_single(qf[0], q[0], group=g, async_op=True),
+                     dist.all_to_all_single(kf[0], k[0], group=g, async_op=True),
+                     dist.all_to_all_single(vf[0], v[0], group=g, async_op=True),
+                     dist.all_gather_into_tensor(alpha.view(-1), gate, group=g, async_op=True)]
+            inbound.append((works, qf, kf, vf, alpha))
+        outbound = []
+        for b in range(B):
+            works, qf, kf, vf, alpha = inbound[b]
+            for w in works:
+                w.wait()
+            o = ops.self_attention(qf, kf, vf, alpha, t_seq_len)
+            inbound[b] = None
+            r = torch.empty(n, s, hp, D, dtype=torch.bfloat16, device=xin.device)
+            outbound.append((dist.all_to_all_single(r, o[0], group=g, async_op=True), r))
+        y = torch.empty(B * s, C, dtype=torch.bfloat16, device=xin.device)
+        for b in range(B):
+            work, r = outbound[b]
+            work.wait()
+            y[b * s:(b + 1) * s] = ops.linear(r.permute(1, 0, 2, 3).reshape(s, C), blk.w_o, blk.b_o)
+        return y
 
     @staticmethod
     def e_block(blk: _Block, e0):

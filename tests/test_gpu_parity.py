@@ -48,6 +48,9 @@ CASES = {
     "unaligned": (1, 5000, 2, 128, 2500, torch.bfloat16, 0.5),
     "all_sparse": (1, 4096, 2, 128, 2048, torch.bfloat16, 0.0),
     "all_flat": (1, 4096, 2, 128, 2048, torch.bfloat16, 1.0),
+    # one exact block per sparse query block (top_k = 1): two steps per tile
+    "topk1_d128": (1, 2048, 8, 128, 1024, torch.bfloat16, 0.5),
+    "topk1_d64": (1, 2048, 8, 64, 1024, torch.bfloat16, 0.5),
 }
 
 
@@ -137,12 +140,20 @@ def test_alpha_tensor_mixed_dtypes(cuda_device):
     assert mx <= MAX_ABS_BF16 and mn <= MEAN_ABS_BF16
 
 
-def test_deterministic(cuda_device):
-    B, S, H, D, t = 1, 4096, 2, 128, 2048
-    q, k, v = (x.cuda() for x in _rand(B, S, H, D, torch.bfloat16, seed=21, t=t))
-    a, _ = run_gpu(q, k, v, t)
-    b, _ = run_gpu(q, k, v, t)
-    assert torch.equal(a, b)
+@pytest.mark.parametrize("shape", [(1, 4096, 2, 128, 2048, torch.bfloat16),
+                                   (2, 2112, 40, 128, 1024, torch.float32),   # top_k = 1, f32 q / k
+                                   (1, 2048, 8, 64, 1024, torch.bfloat16),    # top_k = 1, D = 64
+                                   (1, 8192, 8, 128, 4096, torch.bfloat16)])
+def test_deterministic(cuda_device, shape):
+    """Repeated calls give identical bits (every kernel reduces in a fixed
+    order and waits for all of its tensor-core work before its epilogue)."""
+    B, S, H, D, t, dt = shape
+    q, k, v = (x.cuda() for x in _rand(B, S, H, D, dt, seed=21, t=t))
+    v = v.to(torch.bfloat16)
+    alpha = (torch.rand(B, S, 1, 1, generator=torch.Generator().manual_seed(2)) - 0.5).to(torch.bfloat16).cuda()
+    runs = [run_gpu(q, k, v, t, alpha=alpha)[0] for _ in range(4)]
+    for r in runs[1:]:
+        assert torch.equal(runs[0], r)
 
 
 def test_device_status_clean(cuda_device):
