@@ -94,17 +94,19 @@ def _worker_ulysses_dit(rank, world, port, q):
         latent, source, context = tiny_inputs(cfg)
         seq_len = 2 * 4 * 8 * 17 + 32          # 1120 tokens: target 544 | source 544 | 32 padding
         solo = [dist.new_group([r]) for r in range(world)][rank]
-        sharded = WanDiT(cfg, device="cpu", seed=3, ops=ReferenceOps())
         single = WanDiT(cfg, device="cpu", seed=3, ops=ReferenceOps(), group=solo)
-        assert sharded.world == world and single.world == 1
-        a = sharded.forward(latent, source, 500.0, context, seq_len)
         b = single.forward(latent, source, 500.0, context, seq_len)
-        err = float((a - b).abs().max())
-        scale = float(b.abs().max())
-        q.put((rank, err, scale, tuple(a.shape), bool(torch.isfinite(a).all())))
+        res = []
+        for pipelined in (True, False):
+            sharded = WanDiT(cfg, device="cpu", seed=3, ops=ReferenceOps(), pipelined=pipelined)
+            assert sharded.world == world and single.world == 1
+            a = sharded.forward(latent, source, 500.0, context, seq_len)
+            res.append((float((a - b).abs().max()), float(b.abs().max()), tuple(a.shape),
+                        bool(torch.isfinite(a).all())))
+        q.put((rank, res))
     except Exception as e:  # noqa: BLE001
         import traceback
-        q.put((rank, repr(e) + traceback.format_exc(), None, None, None))
+        q.put((rank, repr(e) + traceback.format_exc()))
     finally:
         if dist.is_initialized():
             dist.destroy_process_group()
@@ -121,9 +123,10 @@ def test_ulysses_step_on_two_ranks_equals_one_rank():
     results = [q.get(timeout=600) for _ in range(world)]
     for p in procs:
         p.join(timeout=60)
-    for rank, err, scale, shape, finite in results:
-        assert scale is not None, err
-        assert shape == (2, 4, 4, 16, 34) and finite
-        # the two runs differ only in GEMM row blocking (bf16 outputs) and the
-        # exchanges, which move bytes unchanged
-        assert err <= 2e-2 * scale, (rank, err, scale)
+    for rank, res in results:
+        assert not isinstance(res, str), res
+        for err, scale, shape, finite in res:      # pipelined, then one exchange per tensor
+            assert shape == (2, 4, 4, 16, 34) and finite
+            # the runs differ only in GEMM row blocking (bf16 outputs) and the
+            # exchanges, which move bytes unchanged
+            assert err <= 2e-2 * scale, (rank, err, scale)
