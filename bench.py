@@ -317,13 +317,18 @@ def run_dit_step(args, world, rank, local):
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local)
+        # the Ulysses exchanges overlap full-GPU kernels: on high-priority
+        # streams their CTAs are scheduled ahead of the compute kernel's
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = not args.dit_normal_priority
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+                                device_id=torch.device("cuda", local), pg_options=opts)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     from wan_dit import WanDiT, WanDiTConfig
     cfg = WanDiTConfig(num_layers=args.dit_layers)
-    model = WanDiT(cfg, device=dev, seed=0, pipelined=not args.dit_no_pipeline)
+    model = WanDiT(cfg, device=dev, seed=0, pipelined=not args.dit_no_pipeline,
+                   pooled_exchange=not args.dit_f32_exchange)
     g = torch.Generator().manual_seed(0)
     shape = (DIT_LATENT[0], args.dit_frames, DIT_LATENT[2], DIT_LATENT[3])
     seq = dit_seq_len(shape)
@@ -390,6 +395,9 @@ def run_dit_step(args, world, rank, local):
                            "parallelism": f"ulysses x{world}",
                            "exchange": "one all-to-all per tensor" if args.dit_no_pipeline or world == 1
                            else "per batch element, overlapped with compute",
+                           "nccl_stream_priority": "normal" if args.dit_normal_priority else "high",
+                           "qk_exchange": "f32" if args.dit_f32_exchange or args.dit_no_pipeline
+                           else "bf16 + f32 block means",
                            "l2": "every step streams 28 GB of weights; no flush"},
                 "roofline": {"bound": "tensor", "kernel": "whole step (cuBLAS GEMMs + this library's kernels)",
                              "achieved": achieved, "peak": sustained, "unit": "TFLOP/s per GPU",
@@ -422,6 +430,10 @@ def main():
     ap.add_argument("--workload", default="480p", choices=list(WORKLOADS) + ["dit-step"])
     ap.add_argument("--dit-layers", type=int, default=40, help="blocks of the DiT step (40 is the A14B model)")
     ap.add_argument("--dit-no-pipeline", action="store_true", help="DiT step: unpipelined Ulysses exchanges")
+    ap.add_argument("--dit-f32-exchange", action="store_true",
+                    help="DiT step: exchange q and k as f32 (default: bf16 with their f32 block means)")
+    ap.add_argument("--dit-normal-priority", action="store_true",
+                    help="DiT step: NCCL on normal-priority streams (default: high priority)")
     ap.add_argument("--dit-frames", type=int, default=DIT_LATENT[1],
                     help="latent frames of the DiT step (21 is 480p video; fewer give a small profiling case)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])

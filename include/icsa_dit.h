@@ -98,6 +98,34 @@ typedef struct icsa_dit_norm_rope_desc {
 ICSA_API int icsa_dit_norm_rope(const icsa_dit_norm_rope_desc* desc, cudaStream_t stream);
 
 /*
+ * The same pass with the attention's block pooling done on the producer side
+ * (the first step of the reference's call, editing_sparse_attention.py:37-55
+ * and :107-111, `compress_seq` of the float32 rotary output): every vector is
+ * written as bf16 (dst_dtype must be ICSA_BF16), and for each vector j with
+ * mean[j] set, the float32 mean of every 64-token block is written too:
+ * rows summed in order and divided by 64, rounded to bf16 values when
+ * round_mean_bf16 is set (the compressed attention then runs in bf16), i.e.
+ * bit for bit what icsa_pool computes from the float32 vector.  Mean of
+ * block k of head h, batch b:
+ *     b*mean_batch_stride + (h / heads_per_group)*mean_group_stride
+ *       + ((h % heads_per_group)*(rows_per_batch/64) + k)*D + d
+ * rows_per_batch must be a multiple of 64.  rs_scratch: float workspace of
+ * count * rows entries (the per-row RMSNorm factors).  A sequence-parallel
+ * caller exchanges bf16 vectors and float32 means instead of float32
+ * vectors, and hands the means to the attention in place of the ones it
+ * would pool from the bf16 values.
+ */
+typedef struct icsa_dit_norm_rope_pool_desc {
+  icsa_dit_norm_rope_desc base;
+  void* mean[3];
+  int64_t mean_batch_stride, mean_group_stride;
+  int round_mean_bf16;
+  float* rs_scratch;
+} icsa_dit_norm_rope_pool_desc;
+
+ICSA_API int icsa_dit_norm_rope_pool(const icsa_dit_norm_rope_pool_desc* desc, cudaStream_t stream);
+
+/*
  * x[r, c] = x[r, c] + y[r, c] * gate[b, c]  in float32 (product and sum
  * rounded separately), b = r / rows_per_batch; gate NULL means x + y.
  *   x: float32 [rows, C] contiguous;  y: bf16 [rows, ldy];  gate: float32,

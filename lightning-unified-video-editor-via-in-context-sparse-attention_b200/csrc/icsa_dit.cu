@@ -263,6 +263,141 @@ __global__ void __launch_bounds__(kRowThreads) norm_rope_kernel(NormRopeArgs a) 
 }
 
 // ---------------------------------------------------------------------------
+// RMSNorm + RoPE with the 64-token block pooling of the result (the producer
+// side of the attention's pooling stage), in two passes:
+//   row_rms_kernel        rs = rsqrt(mean(x^2) + eps) per row, with the same
+//                         arithmetic (and so the same bits) as norm_rope_kernel;
+//   norm_rope_pool_kernel one CTA per (64-token block, 512-column slab,
+//                         vector): each thread owns 8 columns, walks the
+//                         block's 64 rows in order, writes the normalised and
+//                         rotated values as bf16 into the exchange layout and
+//                         sums their float32 values, so the block mean is the
+//                         one the attention's pool_kernel takes of the float32
+//                         result (rows summed in order, / 64, rounded to bf16
+//                         values when the compressed attention runs in bf16).
+// The float32 vectors themselves never reach HBM.
+// ---------------------------------------------------------------------------
+struct RowRmsArgs {
+  const __nv_bfloat16* src[3];
+  float* rs[3];
+  int rows, C;
+  int64_t ld;
+  float eps;
+};
+
+template <int KC>
+__global__ void __launch_bounds__(kRowThreads) row_rms_kernel(RowRmsArgs a) {
+  __shared__ float red[4];
+  const int row = blockIdx.x;
+  const int j = blockIdx.y;
+  // selects instead of a dynamic index, which would copy the arrays to local memory
+  float* rs_out = j == 0 ? a.rs[0] : (j == 1 ? a.rs[1] : a.rs[2]);
+  if (rs_out == nullptr) return;
+  const int tid = threadIdx.x;
+  const __nv_bfloat16* src = (j == 0 ? a.src[0] : (j == 1 ? a.src[1] : a.src[2])) + size_t(row) * a.ld;
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < KC; ++k) {
+    const int col = (k * kRowThreads + tid) * 8;
+    if (col < a.C) {
+      float v[8];
+      load8(src + col, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+    }
+  }
+  const float rs = rsqrtf(block_sum(ss, red) / float(a.C) + a.eps);
+  if (tid == 0) rs_out[row] = rs;
+}
+
+constexpr int kPoolSlab = 512;              // columns per CTA
+constexpr int kPoolThreadsDit = kPoolSlab / 8;
+
+struct RopePoolArgs {
+  NormRopeArgs n;            // sources, weights, rope, bf16 destinations and their strides
+  const float* rs[3];        // per-row rsqrt factors of the normalised vectors
+  float* mean[3];            // f32 block means, or nullptr
+  int64_t mb, mg;            // mean offset of (b, g): b*mb + g*mg + (hl*nbl + blk)*D + d
+  int nbl;                   // 64-token blocks per batch element
+  int round_mean;
+};
+
+__global__ void __launch_bounds__(kPoolThreadsDit) norm_rope_pool_kernel(RopePoolArgs pa) {
+  const NormRopeArgs& a = pa.n;
+  const int j = blockIdx.z;
+  const int b = blockIdx.x / pa.nbl;
+  const int blk = blockIdx.x - b * pa.nbl;
+  const int col = blockIdx.y * kPoolSlab + threadIdx.x * 8;
+  const __nv_bfloat16* w = a.w[j];
+  const float* rs = pa.rs[j];
+  // gate alpha_1 of the block's rows: one thread of the first vector's first slab
+  if (j == 0 && blockIdx.y == 0 && threadIdx.x < 64 && a.gate_src != nullptr) {
+    const int row = b * a.rows_per_batch + blk * 64 + threadIdx.x;
+    const float x = __bfloat162float(a.gate_src[size_t(row) * a.ld]);
+    const float sg = bf16_round(1.f / (1.f + expf(-x)));
+    const float c = bf16_round(sg - 0.5f);
+    a.gate_dst[row] = __float2bfloat16_rn(c * 0.5f);
+  }
+  if (col >= a.C) return;
+  const int h = col / a.D;
+  const int d = col - h * a.D;
+  const int g = h / a.hp;
+  const int hl = h - g * a.hp;
+  const int half = a.D >> 1;
+  float wf[8];
+  if (w != nullptr) load8(w + col, wf);
+  float sum[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sum[i] = 0.f;
+  const bool pool = pa.mean[j] != nullptr;
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.dst[j]) + b * a.sb + g * a.sg + int64_t(hl) * a.D + d;
+#pragma unroll 4
+  for (int r = 0; r < 64; ++r) {
+    const int t_local = blk * 64 + r;
+    const int row = b * a.rows_per_batch + t_local;
+    float n[8];
+    load8(a.src[j] + size_t(row) * a.ld + col, n);
+    if (w != nullptr) {
+      const float f = rs[row];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) n[i] = bf16_round(bf16_round(n[i] * f) * wf[i]);
+    }
+    if (a.rope[j]) {
+      const int t = min(max(a.token_offset + t_local, 0), a.token_count - 1);
+      int4 pos = a.token_pos[t];
+      if (pos.w != 0) {
+        pos.x = min(max(pos.x, 0), a.positions - 1);
+        pos.y = min(max(pos.y, 0), a.positions - 1);
+        pos.z = min(max(pos.z, 0), a.positions - 1);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          const int pair = (d + i) >> 1;
+          const int p = pair < a.split1 ? pos.x : (pair < a.split2 ? pos.y : pos.z);
+          const double2 cs = a.table[size_t(p) * half + pair];
+          const double re = double(n[i]), im = double(n[i + 1]);
+          n[i] = float(re * cs.x - im * cs.y);
+          n[i + 1] = float(re * cs.y + im * cs.x);
+        }
+      }
+    }
+    store8_bf16(dst + int64_t(t_local) * a.st, n);
+    if (pool) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum[i] += n[i];
+    }
+  }
+  if (pool) {
+    float mean[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      mean[i] = sum[i] / 64.f;
+      if (pa.round_mean) mean[i] = bf16_round(mean[i]);
+    }
+    store8_f32(pa.mean[j] + b * pa.mb + g * pa.mg + (int64_t(hl) * pa.nbl + blk) * a.D + d, mean);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Gated residual
 // ---------------------------------------------------------------------------
 struct GateArgs {
@@ -314,39 +449,10 @@ cudaError_t dispatch_chunks(int C, F&& f) {
 }  // namespace
 }  // namespace icsa
 
-using namespace icsa;
-
-extern "C" {
-
-int icsa_dit_modulated_norm(const void* x, int x_dtype, int64_t ldx, int rows, int C, int rows_per_batch,
-                            const float* scale, int64_t scale_batch_stride, const float* shift,
-                            int64_t shift_batch_stride, float eps, int round_norm_bf16, void* out,
-                            cudaStream_t stream) {
-  if (x == nullptr || scale == nullptr || shift == nullptr || out == nullptr)
-    return dit_fail(ICSA_ERR_INVALID, "modulated_norm: NULL buffer");
-  if (x_dtype != ICSA_BF16 && x_dtype != ICSA_F32) return dit_fail(ICSA_ERR_INVALID, "modulated_norm: bad x dtype");
-  if (rows < 0 || C < 8 || C % 8 || C > kMaxChunks * kRowThreads * 8 || rows_per_batch < 1 || ldx < C || ldx % 8)
-    return dit_fail(ICSA_ERR_INVALID, "modulated_norm: rows=%d C=%d ldx=%lld rows_per_batch=%d", rows, C,
-                    (long long)ldx, rows_per_batch);
-  if (scale_batch_stride < 0 || shift_batch_stride < 0 || scale_batch_stride % 4 || shift_batch_stride % 4)
-    return dit_fail(ICSA_ERR_INVALID, "modulated_norm: batch strides must be non-negative multiples of 4");
-  if (!aligned16(x) || !aligned16(scale) || !aligned16(shift) || !aligned16(out))
-    return dit_fail(ICSA_ERR_INVALID, "modulated_norm: buffers must be 16-byte aligned");
-  if (rows == 0) return ICSA_OK;
-  ModNormArgs a{x, ldx, rows, C, rows_per_batch, scale, scale_batch_stride, shift, shift_batch_stride, eps,
-                round_norm_bf16 ? 1 : 0, reinterpret_cast<__nv_bfloat16*>(out)};
-  dispatch_chunks(C, [&](auto kc) {
-    constexpr int KC = decltype(kc)::value;
-    if (x_dtype == ICSA_F32)
-      modulated_norm_kernel<KC, float><<<rows, kRowThreads, 0, stream>>>(a);
-    else
-      modulated_norm_kernel<KC, __nv_bfloat16><<<rows, kRowThreads, 0, stream>>>(a);
-    return cudaSuccess;
-  });
-  return dit_launch_status("modulated_norm launch");
-}
-
-int icsa_dit_norm_rope(const icsa_dit_norm_rope_desc* d, cudaStream_t stream) {
+namespace icsa {
+namespace {
+// Checks a descriptor and fills the kernel arguments.
+int norm_rope_args(const icsa_dit_norm_rope_desc* d, NormRopeArgs& a) {
   if (d == nullptr) return dit_fail(ICSA_ERR_INVALID, "norm_rope: descriptor is NULL");
   if (d->count < 1 || d->count > 3) return dit_fail(ICSA_ERR_INVALID, "norm_rope: count=%d must be 1..3", d->count);
   if (d->rows < 0 || d->D < 8 || d->D % 8 || d->C < d->D || d->C % d->D || d->C > kMaxChunks * kRowThreads * 8 ||
@@ -359,7 +465,7 @@ int icsa_dit_norm_rope(const icsa_dit_norm_rope_desc* d, cudaStream_t stream) {
   if (d->dst_batch_stride % 8 || d->dst_group_stride % 8 || d->dst_token_stride % 8 || d->dst_batch_stride < 0 ||
       d->dst_group_stride < 0 || d->dst_token_stride < 0)
     return dit_fail(ICSA_ERR_INVALID, "norm_rope: destination strides must be non-negative multiples of 8");
-  NormRopeArgs a{};
+  a = NormRopeArgs{};
   a.rows = d->rows; a.C = d->C; a.D = d->D; a.rows_per_batch = d->rows_per_batch; a.token_offset = d->token_offset;
   a.ld = d->ld; a.eps = d->eps; a.hp = d->heads_per_group;
   a.sb = d->dst_batch_stride; a.sg = d->dst_group_stride; a.st = d->dst_token_stride;
@@ -399,6 +505,47 @@ int icsa_dit_norm_rope(const icsa_dit_norm_rope_desc* d, cudaStream_t stream) {
     a.gate_src = reinterpret_cast<const __nv_bfloat16*>(d->gate_src);
     a.gate_dst = reinterpret_cast<__nv_bfloat16*>(d->gate_dst);
   }
+  return ICSA_OK;
+}
+}  // namespace
+}  // namespace icsa
+
+using namespace icsa;
+
+extern "C" {
+
+int icsa_dit_modulated_norm(const void* x, int x_dtype, int64_t ldx, int rows, int C, int rows_per_batch,
+                            const float* scale, int64_t scale_batch_stride, const float* shift,
+                            int64_t shift_batch_stride, float eps, int round_norm_bf16, void* out,
+                            cudaStream_t stream) {
+  if (x == nullptr || scale == nullptr || shift == nullptr || out == nullptr)
+    return dit_fail(ICSA_ERR_INVALID, "modulated_norm: NULL buffer");
+  if (x_dtype != ICSA_BF16 && x_dtype != ICSA_F32) return dit_fail(ICSA_ERR_INVALID, "modulated_norm: bad x dtype");
+  if (rows < 0 || C < 8 || C % 8 || C > kMaxChunks * kRowThreads * 8 || rows_per_batch < 1 || ldx < C || ldx % 8)
+    return dit_fail(ICSA_ERR_INVALID, "modulated_norm: rows=%d C=%d ldx=%lld rows_per_batch=%d", rows, C,
+                    (long long)ldx, rows_per_batch);
+  if (scale_batch_stride < 0 || shift_batch_stride < 0 || scale_batch_stride % 4 || shift_batch_stride % 4)
+    return dit_fail(ICSA_ERR_INVALID, "modulated_norm: batch strides must be non-negative multiples of 4");
+  if (!aligned16(x) || !aligned16(scale) || !aligned16(shift) || !aligned16(out))
+    return dit_fail(ICSA_ERR_INVALID, "modulated_norm: buffers must be 16-byte aligned");
+  if (rows == 0) return ICSA_OK;
+  ModNormArgs a{x, ldx, rows, C, rows_per_batch, scale, scale_batch_stride, shift, shift_batch_stride, eps,
+                round_norm_bf16 ? 1 : 0, reinterpret_cast<__nv_bfloat16*>(out)};
+  dispatch_chunks(C, [&](auto kc) {
+    constexpr int KC = decltype(kc)::value;
+    if (x_dtype == ICSA_F32)
+      modulated_norm_kernel<KC, float><<<rows, kRowThreads, 0, stream>>>(a);
+    else
+      modulated_norm_kernel<KC, __nv_bfloat16><<<rows, kRowThreads, 0, stream>>>(a);
+    return cudaSuccess;
+  });
+  return dit_launch_status("modulated_norm launch");
+}
+
+int icsa_dit_norm_rope(const icsa_dit_norm_rope_desc* d, cudaStream_t stream) {
+  NormRopeArgs a{};
+  const int rc = norm_rope_args(d, a);
+  if (rc != ICSA_OK) return rc;
   if (d->rows == 0) return ICSA_OK;
   const dim3 grid(d->rows, d->count);
   dispatch_chunks(d->C, [&](auto kc) {
@@ -407,6 +554,57 @@ int icsa_dit_norm_rope(const icsa_dit_norm_rope_desc* d, cudaStream_t stream) {
     return cudaSuccess;
   });
   return dit_launch_status("norm_rope launch");
+}
+
+int icsa_dit_norm_rope_pool(const icsa_dit_norm_rope_pool_desc* pd, cudaStream_t stream) {
+  if (pd == nullptr) return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: descriptor is NULL");
+  const icsa_dit_norm_rope_desc* d = &pd->base;
+  NormRopeArgs a{};
+  int rc = norm_rope_args(d, a);
+  if (rc != ICSA_OK) return rc;
+  if (d->rows_per_batch % 64 != 0 || d->rows % d->rows_per_batch != 0)
+    return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: rows_per_batch=%d must be a multiple of 64 dividing rows=%d",
+                    d->rows_per_batch, d->rows);
+  if (d->C % kPoolSlab != 0 && d->C % 8 != 0) return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: C=%d", d->C);
+  if (pd->mean_batch_stride % 4 || pd->mean_group_stride % 4 || pd->mean_batch_stride < 0 ||
+      pd->mean_group_stride < 0)
+    return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: mean strides must be non-negative multiples of 4");
+  RopePoolArgs pa{};
+  pa.n = a;
+  pa.nbl = d->rows_per_batch / 64;
+  pa.mb = pd->mean_batch_stride;
+  pa.mg = pd->mean_group_stride;
+  pa.round_mean = pd->round_mean_bf16 ? 1 : 0;
+  RowRmsArgs ra{};
+  ra.rows = d->rows; ra.C = d->C; ra.ld = d->ld; ra.eps = d->eps;
+  bool any_norm = false;
+  for (int j = 0; j < d->count; ++j) {
+    if (d->dst_dtype[j] != ICSA_BF16)
+      return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: vector %d must be written as bf16", j);
+    if (pd->mean[j] != nullptr && !aligned16(pd->mean[j]))
+      return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: mean %d must be 16-byte aligned", j);
+    pa.mean[j] = reinterpret_cast<float*>(pd->mean[j]);
+    ra.src[j] = a.src[j];
+    if (d->norm_weight[j] != nullptr) {
+      if (pd->rs_scratch == nullptr) return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: rs_scratch is NULL");
+      ra.rs[j] = pd->rs_scratch + size_t(j) * d->rows;
+      pa.rs[j] = ra.rs[j];
+      any_norm = true;
+    }
+  }
+  if (d->rows == 0) return ICSA_OK;
+  if (any_norm) {
+    dispatch_chunks(d->C, [&](auto kc) {
+      constexpr int KC = decltype(kc)::value;
+      row_rms_kernel<KC><<<dim3(d->rows, d->count), kRowThreads, 0, stream>>>(ra);
+      return cudaSuccess;
+    });
+    if ((rc = dit_launch_status("row_rms launch")) != ICSA_OK) return rc;
+  }
+  const int B = d->rows / d->rows_per_batch;
+  const dim3 grid(B * pa.nbl, (d->C + kPoolSlab - 1) / kPoolSlab, d->count);
+  norm_rope_pool_kernel<<<grid, kPoolThreadsDit, 0, stream>>>(pa);
+  return dit_launch_status("norm_rope_pool launch");
 }
 
 int icsa_dit_gated_residual(float* x, const void* y, int64_t ldy, int rows, int C, int rows_per_batch,

@@ -22,7 +22,8 @@ import torch.nn.functional as F
 
 from in_context_sparse_attention import _capi
 
-DIT_EXPORTED = ("icsa_dit_modulated_norm", "icsa_dit_norm_rope", "icsa_dit_gated_residual")
+DIT_EXPORTED = ("icsa_dit_modulated_norm", "icsa_dit_norm_rope", "icsa_dit_norm_rope_pool",
+                "icsa_dit_gated_residual")
 
 _DT = {torch.bfloat16: _capi.ICSA_BF16, torch.float32: _capi.ICSA_F32}
 
@@ -47,6 +48,17 @@ class NormRopeDesc(ctypes.Structure):
     ]
 
 
+class NormRopePoolDesc(ctypes.Structure):
+    """Mirror of struct icsa_dit_norm_rope_pool_desc."""
+    _fields_ = [
+        ("base", NormRopeDesc),
+        ("mean", ctypes.c_void_p * 3),
+        ("mean_batch_stride", ctypes.c_int64), ("mean_group_stride", ctypes.c_int64),
+        ("round_mean_bf16", ctypes.c_int),
+        ("rs_scratch", ctypes.c_void_p),
+    ]
+
+
 def _load():
     lib = _capi.load()
     for name in DIT_EXPORTED:
@@ -57,6 +69,8 @@ def _load():
     lib.icsa_dit_modulated_norm.restype = i
     lib.icsa_dit_norm_rope.argtypes = [ctypes.POINTER(NormRopeDesc), vp]
     lib.icsa_dit_norm_rope.restype = i
+    lib.icsa_dit_norm_rope_pool.argtypes = [ctypes.POINTER(NormRopePoolDesc), vp]
+    lib.icsa_dit_norm_rope_pool.restype = i
     lib.icsa_dit_gated_residual.argtypes = [vp, vp, i64, i, i, i, vp, i64, vp]
     lib.icsa_dit_gated_residual.restype = i
     return lib
@@ -111,6 +125,37 @@ class CudaOps:
         """jobs: up to three (src [rows, C] bf16 view, norm weight or None,
         rope flag, out [B, G, s, hp, D] contiguous).  gate: optional
         (src [rows] bf16 column view, out bf16 [rows])."""
+        d = self._norm_rope_desc(jobs, rows_per_batch, eps, token_offset, table, token_pos, splits, gate)
+        _capi.check(self.lib.icsa_dit_norm_rope(ctypes.byref(d), _stream()), "icsa_dit_norm_rope")
+
+    def norm_rope_pool(self, jobs, means, rows_per_batch, eps, token_offset=0, table=None, token_pos=None,
+                       splits=(0, 0), gate=None, round_mean=True):
+        """norm_rope with bf16 outputs and, for each job whose entry of
+        `means` is a tensor, the f32 means of its 64-token blocks, laid out
+        [B, G, hp, s/64, D] (include/icsa_dit.h, icsa_dit_norm_rope_pool)."""
+        base = self._norm_rope_desc(jobs, rows_per_batch, eps, token_offset, table, token_pos, splits, gate)
+        B, G, s, hp, D = jobs[0][3].shape
+        if s % 64:
+            raise ValueError(f"norm_rope_pool: {s} tokens per batch element are not whole 64-token blocks")
+        d = NormRopePoolDesc()
+        d.base = base
+        ref = None
+        for j, m in enumerate(means):
+            if m is None:
+                continue
+            if m.shape != (B, G, hp, s // 64, D) or m.dtype != torch.float32 or not m.is_contiguous():
+                raise ValueError(f"norm_rope_pool: mean {j} must be contiguous f32 {(B, G, hp, s // 64, D)}")
+            d.mean[j] = m.data_ptr()
+            ref = m
+        if ref is not None:
+            d.mean_batch_stride, d.mean_group_stride = ref.stride(0), ref.stride(1)
+        d.round_mean_bf16 = int(bool(round_mean))
+        rs = torch.empty(len(jobs) * B * s, dtype=torch.float32, device=jobs[0][0].device)
+        d.rs_scratch = rs.data_ptr()
+        _capi.check(self.lib.icsa_dit_norm_rope_pool(ctypes.byref(d), _stream()), "icsa_dit_norm_rope_pool")
+
+    @staticmethod
+    def _norm_rope_desc(jobs, rows_per_batch, eps, token_offset, table, token_pos, splits, gate):
         d = NormRopeDesc()
         src0 = jobs[0][0]
         rows, ld = _rows(src0)
@@ -148,7 +193,7 @@ class CudaOps:
             if gsrc.stride(0) != ld:
                 raise ValueError("norm_rope: the gate column must share the rows' leading dimension")
             d.gate_src, d.gate_dst = gsrc.data_ptr(), gout.data_ptr()
-        _capi.check(self.lib.icsa_dit_norm_rope(ctypes.byref(d), _stream()), "icsa_dit_norm_rope")
+        return d
 
     def gated_residual_(self, x, y, gate, rows_per_batch):
         """x (f32 [rows, C], in place) += y (bf16 [rows, C] view) * gate[b] (f32 [B, C] or None)."""
@@ -167,20 +212,23 @@ class CudaOps:
         return x
 
     # --- attention ---------------------------------------------------------
-    def self_attention(self, q, k, v, alpha, t_seq_len):
+    def self_attention(self, q, k, v, alpha, t_seq_len, means=None):
         """In-context sparse attention of the reference's WanSelfAttention
         (model.py:172-173) for q, k f32 and v bf16 [B, S, h, D] and the bf16
         gate alpha [B, S], returned as the bf16 operand of the output
         projection (the reference's f32 result rounded once to bf16, which is
-        what its autocast o-projection reads)."""
+        what its autocast o-projection reads).
+
+        means: optional (qmean, kmean) f32 [B, h, NB, D], the block means of
+        the f32 q and k that were rounded to the bf16 q and k passed here
+        (icsa_dit_norm_rope_pool computes them before the exchange).  The
+        pool stage then runs on the bf16 tensors, its q / k means are
+        replaced by these, and the result is bit for bit the one of the f32
+        call."""
+        if means is not None:
+            return self._self_attention_premeaned(q, k, v, alpha, t_seq_len, means)
         B, S, H, D = q.shape
-        p = _capi.problem(B, S, H, D, int(t_seq_len))
-        p.q_dtype, p.k_dtype, p.v_dtype = _DT[q.dtype], _DT[k.dtype], _DT[v.dtype]
-        p.out_dtype = _capi.ICSA_BF16
-        p.outc_bf16, p.ca_bf16 = 1, 1
-        p.alpha_mode, p.alpha_dtype = _capi.ICSA_ALPHA_TENSOR, _DT[alpha.dtype]
-        for i, st in enumerate((alpha.stride(0), alpha.stride(1), 0, 0)):
-            p.alpha_strides[i] = st
+        p = self._problem(q, k, v, alpha, t_seq_len, _DT[q.dtype], _DT[k.dtype])
         lib = self.lib
         size = lib.icsa_workspace_size(ctypes.byref(p))
         if size == 0:
@@ -189,6 +237,42 @@ class CudaOps:
         out = torch.empty(B, S, H, D, dtype=torch.bfloat16, device=q.device)
         _capi.check(lib.icsa_forward(ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), alpha.data_ptr(),
                                      out.data_ptr(), ws.data_ptr(), size, _stream()), "icsa_forward")
+        return out
+
+    def _problem(self, q, k, v, alpha, t_seq_len, q_dtype, k_dtype):
+        B, S, H, D = q.shape
+        p = _capi.problem(B, S, H, D, int(t_seq_len))
+        p.q_dtype, p.k_dtype, p.v_dtype = q_dtype, k_dtype, _DT[v.dtype]
+        p.out_dtype = _capi.ICSA_BF16
+        p.outc_bf16, p.ca_bf16 = 1, 1
+        p.alpha_mode, p.alpha_dtype = _capi.ICSA_ALPHA_TENSOR, _DT[alpha.dtype]
+        for i, st in enumerate((alpha.stride(0), alpha.stride(1), 0, 0)):
+            p.alpha_strides[i] = st
+        return p
+
+    def _self_attention_premeaned(self, q, k, v, alpha, t_seq_len, means):
+        B, S, H, D = q.shape
+        if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+            raise ValueError("self_attention with means: q and k must be the bf16 tensors")
+        p = self._problem(q, k, v, alpha, t_seq_len, _capi.ICSA_BF16, _capi.ICSA_BF16)
+        L = _capi.workspace_layout(p)
+        NB = p.num_blocks
+        qm, km = means
+        if qm.shape != (B, H, NB, D) or km.shape != (B, H, NB, D):
+            raise ValueError(f"self_attention means must be f32 [{B}, {H}, {NB}, {D}]")
+        lib, st = self.lib, _stream()
+        size = L.total
+        ws = torch.empty(size, dtype=torch.uint8, device=q.device)
+        out = torch.empty(B, S, H, D, dtype=torch.bfloat16, device=q.device)
+        pp = ctypes.byref(p)
+        a = (q.data_ptr(), k.data_ptr(), v.data_ptr())
+        _capi.check(lib.icsa_pool(pp, *a, ws.data_ptr(), size, st), "icsa_pool")
+        n = B * H * NB * D * 4
+        ws[L.qmean:L.qmean + n].view(torch.float32).copy_(qm.reshape(-1))
+        ws[L.kmean:L.kmean + n].view(torch.float32).copy_(km.reshape(-1))
+        _capi.check(lib.icsa_select(pp, a[1], a[2], ws.data_ptr(), size, st), "icsa_select")
+        _capi.check(lib.icsa_attend(pp, *a, alpha.data_ptr(), out.data_ptr(), ws.data_ptr(), size, st),
+                    "icsa_attend")
         return out
 
     @staticmethod

@@ -292,16 +292,21 @@ def result_dtypes(q_dtype, k_dtype, v_dtype, alpha):
 
 
 def editing_sparse_attention(q, k, v, t_seq_len, alpha_2=1.0, sparsity=0.0625, select_ratio=0.125,
-                             flat_ratio=0.5, forced=None) -> OracleResult:
+                             flat_ratio=0.5, forced=None, means=None) -> OracleResult:
     """The whole call on the CPU.  forced: optional dict with 'sel', 'order',
     'sparse_idx' from another implementation; when given, those selections are
     used instead of the oracle's own (so outputs can be compared without
-    near-tie selection differences)."""
+    near-tie selection differences).  means: optional (qm, km) [B, NB, H, D]
+    block means of the float32 q and k that the given bf16 q and k were
+    rounded from (a sequence-parallel caller pools before it exchanges the
+    bf16 tensors); they replace the means of q and k."""
     B, S, H, D = q.shape
     c = Counts.make(B, S, H, D, t_seq_len, sparsity, select_ratio, flat_ratio)
     outc_dt, ca_dt, out_dt = result_dtypes(q.dtype, k.dtype, v.dtype, alpha_2)
 
     qm, km, vm = block_means(q), block_means(k), block_means(v)
+    if means is not None:
+        qm, km = means
     cast = (lambda t: t.to(torch.bfloat16)) if outc_dt == torch.bfloat16 else (lambda t: t)
     s, P, out_c = compressed_attention(*(cast(t).permute(0, 2, 1, 3) for t in (qm, km, vm)))
     colsum = incontext_keys(P, c.n_t)

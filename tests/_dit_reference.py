@@ -106,6 +106,29 @@ class ReferenceOps:
             gsrc, gout = gate
             gout.copy_((gsrc.sigmoid() - 0.5) * 0.5)
 
+    def norm_rope_pool(self, jobs, means, rows_per_batch, eps, token_offset=0, table=None, token_pos=None,
+                       splits=(0, 0), gate=None, round_mean=True):
+        """norm_rope computed in f32, written as bf16, and the 64-token block
+        means of the f32 values (compress_seq, editing_sparse_attention.py:
+        37-55 of the reference), laid out [B, G, hp, s/64, D]."""
+        f32 = []
+        for src, w, rope, out in jobs:
+            tmp = torch.empty(out.shape, dtype=torch.float32, device=out.device)
+            f32.append(tmp)
+            self.norm_rope([(src, w, rope, tmp)], rows_per_batch, eps, token_offset, table, token_pos, splits)
+            out.copy_(tmp.to(out.dtype))
+        if gate is not None:
+            gsrc, gout = gate
+            gout.copy_((gsrc.sigmoid() - 0.5) * 0.5)
+        for x, m in zip(f32, means):
+            if m is None:
+                continue
+            B, G, s, hp, D = x.shape
+            mm = x.reshape(B, G, s // 64, 64, hp, D).sum(dim=3) / 64.0
+            if round_mean:
+                mm = mm.to(torch.bfloat16).float()
+            m.copy_(mm.permute(0, 1, 3, 2, 4))
+
     def gated_residual_(self, x, y, gate, rows_per_batch):
         if gate is None:
             x.copy_(x + y)
@@ -113,11 +136,14 @@ class ReferenceOps:
             x.copy_(x + y * self._per_row(gate, x.shape[0], rows_per_batch))
         return x
 
-    def self_attention(self, q, k, v, alpha, t_seq_len):
+    def self_attention(self, q, k, v, alpha, t_seq_len, means=None):
         if self._attention is not None:
+            if means is not None:
+                return self._attention(q, k, v, alpha, t_seq_len, means=means)
             return self._attention(q, k, v, alpha, t_seq_len)
+        m = None if means is None else tuple(x.cpu().permute(0, 2, 1, 3) for x in means)
         r = icsa_oracle.editing_sparse_attention(q.cpu(), k.cpu(), v.cpu(), t_seq_len,
-                                                 alpha_2=alpha.cpu()[:, :, None, None])
+                                                 alpha_2=alpha.cpu()[:, :, None, None], means=m)
         return r.out.to(torch.bfloat16).to(q.device).contiguous()
 
     @staticmethod

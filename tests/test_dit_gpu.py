@@ -188,3 +188,50 @@ def test_full_width_block_matches_reference_block_math(ops):
     assert got.shape == (2, cfg.out_dim, 2, 32, 64) and bool(torch.isfinite(got).all())
     assert grid == (2, 16, 32)
     assert_step_close(got, ref)
+
+
+@pytest.mark.parametrize("grid,S,t_aligned", [((4, 16, 32), 4096, True), ((3, 10, 17), 1024, False)])
+def test_pooled_qk_give_the_f32_call_bit_for_bit(ops, grid, S, t_aligned):
+    """The sequence-parallel exchange sends q and k as bf16 with the f32
+    means of their 64-token blocks: the means equal those the pool stage
+    takes of the f32 tensors, and the attention's output equals the f32
+    call's bit for bit (aligned and unaligned t_seq_len)."""
+    from wan_dit import head_dim_splits, rope_table, token_positions
+    from _helpers import region
+    from in_context_sparse_attention import editing_sparse_attention
+    B, H, D = 1, 8, 128
+    C = H * D
+    t = grid[0] * grid[1] * grid[2]
+    assert (t % 64 == 0) == t_aligned
+    g = torch.Generator(device="cuda").manual_seed(11)
+    qkv = torch.randn(B * S, 3 * C + 8, generator=g, device="cuda").to(torch.bfloat16)
+    wq = (1 + 0.1 * torch.randn(C, generator=g, device="cuda")).to(torch.bfloat16)
+    wk = (1 + 0.1 * torch.randn(C, generator=g, device="cuda")).to(torch.bfloat16)
+    table, pos, splits = rope_table(D).cuda(), token_positions(grid, grid, S).cuda(), head_dim_splits(D)
+    jobs = lambda q, k, v: [(qkv[:, :C], wq, True, q), (qkv[:, C:2 * C], wk, True, k),  # noqa: E731
+                            (qkv[:, 2 * C:3 * C], None, False, v)]
+    q32 = torch.empty(B, 1, S, H, D, device="cuda")
+    k32 = torch.empty_like(q32)
+    v_a = torch.empty(B, 1, S, H, D, dtype=torch.bfloat16, device="cuda")
+    gate_a = torch.empty(B * S, dtype=torch.bfloat16, device="cuda")
+    ops.norm_rope(jobs(q32, k32, v_a), rows_per_batch=S, eps=1e-6, table=table, token_pos=pos, splits=splits,
+                  gate=(qkv[:, 3 * C], gate_a))
+    qb, kb, v_b = (torch.empty(B, 1, S, H, D, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+    qm = torch.empty(B, 1, H, S // 64, D, device="cuda")
+    km = torch.empty_like(qm)
+    gate_b = torch.empty(B * S, dtype=torch.bfloat16, device="cuda")
+    ops.norm_rope_pool(jobs(qb, kb, v_b), [qm, km, None], rows_per_batch=S, eps=1e-6, table=table, token_pos=pos,
+                       splits=splits, gate=(qkv[:, 3 * C], gate_b))
+    assert torch.equal(qb, q32.to(torch.bfloat16)) and torch.equal(kb, k32.to(torch.bfloat16))
+    assert torch.equal(v_a, v_b) and torch.equal(gate_a, gate_b)
+    # the means are the pool stage's means of the f32 tensors
+    dbg = {}
+    editing_sparse_attention(q32.view(B, S, H, D), k32.view(B, S, H, D), v_a.view(B, S, H, D), t, S - t, _debug=dbg)
+    NB = S // 64
+    assert torch.equal(qm.view(B, H, NB, D), region(dbg, "qmean", torch.float32, (B, H, NB, D)))
+    assert torch.equal(km.view(B, H, NB, D), region(dbg, "kmean", torch.float32, (B, H, NB, D)))
+    alpha = gate_a.view(B, S)
+    out_a = ops.self_attention(q32.view(B, S, H, D), k32.view(B, S, H, D), v_a.view(B, S, H, D), alpha, t)
+    out_b = ops.self_attention(qb.view(B, S, H, D), kb.view(B, S, H, D), v_b.view(B, S, H, D), alpha, t,
+                               means=(qm.view(B, H, NB, D), km.view(B, H, NB, D)))
+    assert torch.equal(out_a, out_b)

@@ -92,13 +92,15 @@ def _worker_ulysses_dit(rank, world, port, q):
         from _dit_reference import ReferenceOps
         cfg = WanDiTConfig(**TINY)
         latent, source, context = tiny_inputs(cfg)
-        seq_len = 2 * 4 * 8 * 17 + 32          # 1120 tokens: target 544 | source 544 | 32 padding
+        seq_len = 2 * 4 * 8 * 17 + 64          # 1152 tokens: target 544 | source 544 | 64 padding
+        assert (seq_len // world) % 64 == 0     # whole 64-token blocks per rank: the pooled exchange applies
         solo = [dist.new_group([r]) for r in range(world)][rank]
         single = WanDiT(cfg, device="cpu", seed=3, ops=ReferenceOps(), group=solo)
         b = single.forward(latent, source, 500.0, context, seq_len)
         res = []
-        for pipelined in (True, False):
-            sharded = WanDiT(cfg, device="cpu", seed=3, ops=ReferenceOps(), pipelined=pipelined)
+        for pipelined, pooled in ((True, True), (True, False), (False, False)):
+            sharded = WanDiT(cfg, device="cpu", seed=3, ops=ReferenceOps(), pipelined=pipelined,
+                             pooled_exchange=pooled)
             assert sharded.world == world and single.world == 1
             a = sharded.forward(latent, source, 500.0, context, seq_len)
             res.append((float((a - b).abs().max()), float(b.abs().max()), tuple(a.shape),
@@ -125,7 +127,7 @@ def test_ulysses_step_on_two_ranks_equals_one_rank():
         p.join(timeout=60)
     for rank, res in results:
         assert not isinstance(res, str), res
-        for err, scale, shape, finite in res:      # pipelined, then one exchange per tensor
+        for err, scale, shape, finite in res:      # pipelined (pooled, f32), then one exchange per tensor
             assert shape == (2, 4, 4, 16, 34) and finite
             # the runs differ only in GEMM row blocking (bf16 outputs) and the
             # exchanges, which move bytes unchanged
