@@ -565,7 +565,6 @@ int icsa_dit_norm_rope_pool(const icsa_dit_norm_rope_pool_desc* pd, cudaStream_t
   if (d->rows_per_batch % 64 != 0 || d->rows % d->rows_per_batch != 0)
     return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: rows_per_batch=%d must be a multiple of 64 dividing rows=%d",
                     d->rows_per_batch, d->rows);
-  if (d->C % kPoolSlab != 0 && d->C % 8 != 0) return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: C=%d", d->C);
   if (pd->mean_batch_stride % 4 || pd->mean_group_stride % 4 || pd->mean_batch_stride < 0 ||
       pd->mean_group_stride < 0)
     return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: mean strides must be non-negative multiples of 4");

@@ -382,7 +382,11 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
     }
     tc::tmem_wait_st();
     tc::fence_before_sync();
-    mbar_arrive(&sm.p_full[j & 1]);
+    // one arrive per warp (count 4): its lanes' TMEM stores are complete
+    // (wait::st) and ordered before the elected arrive by __syncwarp
+    __syncwarp();
+    if ((tid & 31) == 0) mbar_arrive(&sm.p_full[j & 1]);
+    __syncwarp();
   }
 
   // epilogue: (acc * f + g_acc) / (l * f + g_l), f re-bases acc and l on the final max.
@@ -508,8 +512,8 @@ __global__ void __launch_bounds__(kSThreads, 1) sparse_kernel(const AttnParams p
     }
     mbar_init(&sm.s_full[0], 1);
     mbar_init(&sm.s_full[1], 1);
-    mbar_init(&sm.p_full[0], 128);
-    mbar_init(&sm.p_full[1], 128);
+    mbar_init(&sm.p_full[0], 4);
+    mbar_init(&sm.p_full[1], 4);
     mbar_init(&sm.pv_done, 1);
     mbar_init(&sm.mma_fin, 1);
     sm.abort_flag = 0;
