@@ -26,10 +26,21 @@ namespace {
 // 128x128 output tile per CTA, 256 threads, 8x8 outputs per thread (rows and
 // columns split into two groups of 4, 64 apart, so that the float4 reads of
 // shared memory are conflict-free).  Every output accumulates over k in
-// increasing order with fmaf, then divides by sqrt(D).
+// increasing order with fmaf-rounded FMAs (two outputs per f32x2
+// instruction), then divides by sqrt(D).
 // ---------------------------------------------------------------------------
 constexpr int kGT = 128;  // GEMM tile
 constexpr int kGK = 8;    // GEMM k-chunk
+
+// Two independent fp32 FMAs in one packed instruction (sm_100 f32x2):
+// x = a0 * b0 + x, y = a1 * b1 + y, each rounded as fmaf rounds it, so every
+// output still accumulates over k in the same order with the same bits.
+ICSA_DEV void fma_x2(float& x, float& y, float a0, float a1, float b0, float b1) {
+  asm("{.reg .b64 a, b, c;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%0, %1};\n\t"
+      "fma.rn.f32x2 c, a, b, c;\n\tmov.b64 {%0, %1}, c;}"
+      : "+f"(x), "+f"(y)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
 
 __global__ void __launch_bounds__(256) scores_kernel(SelectParams p) {
   __shared__ __align__(16) float As[kGK][kGT + 4];
@@ -61,7 +72,7 @@ __global__ void __launch_bounds__(256) scores_kernel(SelectParams p) {
 #pragma unroll
       for (int u = 0; u < 8; ++u)
 #pragma unroll
-        for (int w = 0; w < 8; ++w) acc[u][w] = fmaf(a[u], b[w], acc[u][w]);
+        for (int w = 0; w < 8; w += 2) fma_x2(acc[u][w], acc[u][w + 1], a[u], a[u], b[w], b[w + 1]);
     }
     __syncthreads();
   }
@@ -192,7 +203,7 @@ __global__ void __launch_bounds__(256) outc_kernel(SelectParams p) {
 #pragma unroll
       for (int u = 0; u < 4; ++u)
 #pragma unroll
-        for (int w = 0; w < kCW; ++w) acc[u][w] = fmaf(av[u], b[w], acc[u][w]);
+        for (int w = 0; w < kCW; w += 2) fma_x2(acc[u][w], acc[u][w + 1], av[u], av[u], b[w], b[w + 1]);
     }
     __syncthreads();
   }
