@@ -1,7 +1,7 @@
 """Benchmark of the in-context sparse attention call (BASELINE metric:
 "sparse-attn ms/call at 65K joint tokens (40h x 128d bf16) 1/2/4/8 GPU").
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload 480p|720p|config1|dit-step]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload 480p|720p|config1|dit-step|sweep]
                     [--impl b200|reference]
 
 One step is one whole call over all 40 heads.  With N GPUs (torchrun, one
@@ -167,10 +167,10 @@ class ClockSampler:
 # device-resident runner through the stage entry points of the C ABI
 # ---------------------------------------------------------------------------
 class Runner:
-    def __init__(self, q, k, v, t_seq_len):
+    def __init__(self, q, k, v, t_seq_len, select_ratio=0.125, flat_ratio=0.5):
         self.lib = _capi.load()
         B, S, H, D = q.shape
-        self.p = _capi.problem(B, S, H, D, t_seq_len)
+        self.p = _capi.problem(B, S, H, D, t_seq_len, select_ratio=select_ratio, flat_ratio=flat_ratio)
         self.L = _capi.workspace_layout(self.p)
         self.size = self.lib.icsa_workspace_size(ctypes.byref(self.p))
         self.ws = torch.empty(self.size, dtype=torch.uint8, device=q.device)
@@ -415,6 +415,76 @@ def run_dit_step(args, world, rank, local):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# stage sweep: every stage timed on its own over joint
+# length x flat ratio x source-selection ratio x batch, 40 heads x 128 d bf16
+# ---------------------------------------------------------------------------
+SWEEP_GRIDS = {4096: (4, 32, 32), 8192: (8, 32, 32), 16384: (16, 32, 32), 32768: (21, 30, 52),
+               65536: (16, 64, 64)}  # tokens per video -> latent grid of the blurred-field generator
+SWEEP_FLAT = (0.0, 0.5, 1.0)
+SWEEP_SRR = (0.0625, 0.125, 0.25)
+SWEEP_BATCH = (1, 2)
+
+
+def run_sweep(args, local):
+    """One JSON line with a row per configuration: the median CUDA-event time
+    of each stage (pool, select, attend_dense, attend_sparse) over K steps
+    after W warm-up steps, with each stage's achieved rate against the
+    measured peaks (HBM GB/s for the pooling pass, TFLOP/s for the two
+    attention kernels; the selection stage is latency-bound and reported in
+    ms).  Inputs of one (joint length, batch) pair are generated once and
+    shared by its flat-ratio / selection-ratio rows."""
+    import dataclasses
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    sustained, burst, hbm, src = peaks()
+    halves = [h for h in SWEEP_GRIDS if not args.sweep_max_joint or 2 * h <= args.sweep_max_joint]
+    rows, launches = [], 0
+    for half in halves:
+        for B in SWEEP_BATCH:
+            w = dataclasses.replace(synthetic.WAN480P, name=f"sweep_joint{2 * half}_b{B}", B=B,
+                                    grid=SWEEP_GRIDS[half], half_len=half)
+            q, k, v = synthetic.make_inputs(w, device=dev)
+            for fr in SWEEP_FLAT:
+                for srr in SWEEP_SRR:
+                    r = Runner(q, k, v, half, select_ratio=srr, flat_ratio=fr)
+                    for _ in range(args.warmup):
+                        r.step()
+                    torch.cuda.synchronize()
+                    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+                    for i in range(args.steps):
+                        r.step(evs[i])
+                    torch.cuda.synchronize()
+                    _capi.check(r.lib.icsa_device_status(r.ws.data_ptr(), torch.cuda.current_stream().cuda_stream),
+                                "icsa_device_status")
+                    st = {n: statistics.median(e[j].elapsed_time(e[j + 1]) for e in evs) for j, n in
+                          enumerate(("pool", "select", "attend_dense", "attend_sparse"))}
+                    _, fl, sp = attention_flops(r.p, r.L.n_sparse)
+                    p = r.p
+                    pool_bytes = 3 * q.numel() * q.element_size() + 3 * B * w.H * p.num_blocks * w.D * 6
+                    row = {"joint": 2 * half, "B": B, "flat_ratio": fr, "select_ratio": srr,
+                           "num_flat": p.num_flat, "n_sparse": r.L.n_sparse, "topK": p.topK, "top_k": p.top_k,
+                           "tkv": p.tkv, "ms": st, "ms_call": sum(st.values()),
+                           "pool_gbs": pool_bytes / (st["pool"] * 1e-3) / 1e9,
+                           "dense_tflops": fl / (st["attend_dense"] * 1e-3) / 1e12 if fl else None,
+                           "sparse_tflops": sp / (st["attend_sparse"] * 1e-3) / 1e12 if sp else None}
+                    row["pool_frac"] = row["pool_gbs"] / hbm
+                    row["dense_frac"] = row["dense_tflops"] / sustained if fl else None
+                    row["sparse_frac"] = row["sparse_tflops"] / sustained if sp else None
+                    rows.append(row)
+                    # pool, scores, rowstats, outc, colsum, 2 sorts, extended KV; top-k and the sparse kernel only with
+                    # sparse blocks, the dense kernel only with flat blocks
+                    launches += (8 + (2 if r.L.n_sparse else 0) + (1 if p.num_flat else 0)) * args.steps
+                    del r
+            del q, k, v
+            torch.cuda.empty_cache()
+    print(json.dumps({"workload": "stage-sweep", "unit": "ms", "steps": args.steps, "warmup": args.warmup,
+                      "dtype": "bf16", "data": "synthetic (seeded blurred-field generator)", "H": 40, "D": 128,
+                      "peaks": {"hbm_gbs": hbm, "bf16_tflops_sustained": sustained, "kind": src},
+                      "l2": "inputs of 0.13-10.7 GB; the small joint lengths fit in L2 (no flush)",
+                      "gpu_launches": launches, "rows": rows}), flush=True)
+
+
 def config_dict(w, n):
     return {"workload": w.name, "B": w.B, "H": w.H, "D": w.D, "S": w.S, "t_seq_len": w.t_seq_len,
             "grid": list(w.grid), "heads_per_gpu": w.H // n, "parallelism": f"head-sharded x{n}",
@@ -427,7 +497,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="480p", choices=list(WORKLOADS) + ["dit-step"])
+    ap.add_argument("--workload", default="480p", choices=list(WORKLOADS) + ["dit-step", "sweep"])
+    ap.add_argument("--sweep-max-joint", type=int, default=0, help="sweep: largest joint length (0: all)")
     ap.add_argument("--dit-layers", type=int, default=40, help="blocks of the DiT step (40 is the A14B model)")
     ap.add_argument("--dit-no-pipeline", action="store_true", help="DiT step: unpipelined Ulysses exchanges")
     ap.add_argument("--dit-f32-exchange", action="store_true",
@@ -451,6 +522,10 @@ def main():
         return
     if args.workload == "dit-step":
         run_dit_step(args, world, rank, local)
+        return
+    if args.workload == "sweep":
+        if rank == 0:
+            run_sweep(args, local)
         return
 
     import datetime
