@@ -11,7 +11,10 @@ maximum over ranks: total work per call is fixed, so scaling is "strong".
 
 * value: ms per call with q/k/v resident in HBM, timed with CUDA events on
   the launching stream around exactly K steps (barrier + synchronize on both
-  sides, max over ranks); the inputs (2 GB) are larger than L2.
+  sides, max over ranks); the inputs (2 GB) are larger than L2.  A step goes
+  through the stage entry points with the two attention halves overlapped as
+  icsa_attend overlaps them; stages_ms.attend_sparse and sequential_call come
+  from the same calls with the halves in sequence, after the timed region.
 * e2e: the same call through the public Python API on pinned host q/k/v
   and a pinned host result: the library streams groups of heads through the
   GPU, so every input and output byte crosses PCIe inside the timed region
@@ -176,9 +179,18 @@ class Runner:
         self.ws = torch.empty(self.size, dtype=torch.uint8, device=q.device)
         self.out = torch.empty_like(q)
         self.q, self.k, self.v = q, k, v
+        self.side = torch.cuda.Stream(device=q.device)
+        self.fork, self.join = torch.cuda.Event(), torch.cuda.Event()
 
-    def step(self, ev=None):
-        lib, pp, st = self.lib, ctypes.byref(self.p), torch.cuda.current_stream().cuda_stream
+    def step(self, ev=None, overlap=True):
+        """One call through the stage entry points.  With `overlap` the two
+        attention halves run as icsa_attend runs them: the dense kernel first
+        on the current stream, the block-sparse kernel on a side stream that
+        forks after the selection and joins before the next call, so sparse
+        CTAs fill the SMs of the dense kernel's last wave.  ev[3] (after the
+        dense launch, on its stream) times the dense kernel."""
+        lib, pp, cur = self.lib, ctypes.byref(self.p), torch.cuda.current_stream()
+        st = cur.cuda_stream
         a = (self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr())
         if ev is not None:
             ev[0].record()
@@ -188,12 +200,20 @@ class Runner:
         _capi.check(lib.icsa_select(pp, a[1], a[2], self.ws.data_ptr(), self.size, st), "icsa_select")
         if ev is not None:
             ev[2].record()
+        both = overlap and self.p.num_flat > 0 and self.L.n_sparse > 0
+        if both:
+            self.fork.record(cur)
+            self.side.wait_event(self.fork)
         _capi.check(lib.icsa_attend_dense(pp, *a, None, self.out.data_ptr(), self.ws.data_ptr(), self.size, st),
                     "icsa_attend_dense")
         if ev is not None:
             ev[3].record()
-        _capi.check(lib.icsa_attend_sparse(pp, *a, None, self.out.data_ptr(), self.ws.data_ptr(), self.size, st),
+        sst = self.side.cuda_stream if both else st
+        _capi.check(lib.icsa_attend_sparse(pp, *a, None, self.out.data_ptr(), self.ws.data_ptr(), self.size, sst),
                     "icsa_attend_sparse")
+        if both:
+            self.join.record(self.side)
+            cur.wait_event(self.join)
         if ev is not None:
             ev[4].record()
 
@@ -449,11 +469,11 @@ def run_sweep(args, local):
                 for srr in SWEEP_SRR:
                     r = Runner(q, k, v, half, select_ratio=srr, flat_ratio=fr)
                     for _ in range(args.warmup):
-                        r.step()
+                        r.step(overlap=False)
                     torch.cuda.synchronize()
                     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
                     for i in range(args.steps):
-                        r.step(evs[i])
+                        r.step(evs[i], overlap=False)
                     torch.cuda.synchronize()
                     _capi.check(r.lib.icsa_device_status(r.ws.data_ptr(), torch.cuda.current_stream().cuda_stream),
                                 "icsa_device_status")
@@ -568,7 +588,15 @@ def main():
     clk = clocks.stop()
     elapsed = t_start.elapsed_time(t_end)
     stage = {n: statistics.mean(e[i].elapsed_time(e[i + 1]) for e in evs) for i, n in
-             enumerate(("pool", "select", "attend_dense", "attend_sparse"))}
+             enumerate(("pool", "select", "attend_dense", "attend_sparse_exposed"))}
+    # the block-sparse kernel on its own: the same calls with the two attention
+    # halves in sequence, after the timed region
+    seq = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    for i in range(args.steps):
+        runner.step(seq[i], overlap=False)
+    torch.cuda.synchronize()
+    stage["attend_sparse"] = statistics.mean(e[3].elapsed_time(e[4]) for e in seq)
+    stage["sequential_call"] = statistics.mean(e[0].elapsed_time(e[4]) for e in seq)
     rc = runner.lib.icsa_device_status(runner.ws.data_ptr(), torch.cuda.current_stream().cuda_stream)
     _capi.check(rc, "icsa_device_status")
 

@@ -13,6 +13,12 @@
  *   - q, k, v and the output are contiguous [B, S, H, D] device buffers.
  *   - Every call is asynchronous on `stream` and performs no host
  *     synchronisation; it can be captured into a CUDA graph.
+ *   - icsa_select and icsa_attend (and so icsa_forward) run part of their
+ *     kernels on a second stream of the library's own, forked from `stream`
+ *     and joined back to it by events: work enqueued on `stream` after the
+ *     call still runs after all of it.  The library creates that stream and
+ *     its two events on the first such call on each device; make that first
+ *     call before any stream capture.
  *   - Every function returns an icsa_status; on failure
  *     icsa_last_error() returns a message for the calling thread.
  *   - Scratch memory ("workspace") is provided by the caller; its size comes

@@ -7,6 +7,7 @@
 #include <cmath>
 #include <string>
 #include <algorithm>
+#include <mutex>
 
 #include "icsa_kernels.cuh"
 
@@ -182,6 +183,59 @@ int check_call(const icsa_problem* p, void* ws, size_t ws_bytes, icsa_workspace_
   return ICSA_OK;
 }
 
+// ---------------------------------------------------------------------------
+// A second stream per device for the parts of one call that may run side by
+// side: out_compress beside the selection chain, and the block-sparse
+// attention beside the dense attention (its CTAs take the SMs that the dense
+// kernel's last wave leaves idle).  Side work is ordered by events: the side
+// stream waits for an event recorded on the caller's stream, and the caller's
+// stream waits for an event recorded after the side work, so the caller sees
+// one ordered call and a captured caller stream captures the side work too.
+// The stream and events are created by the first call on a device.  The
+// mutex keeps host threads from interleaving their use of the two events.
+// ---------------------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_side_mutex;
+SideStream g_side[kMaxDevices];
+
+// Called with g_side_mutex held.
+int side_stream(SideStream** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(ICSA_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  SideStream& s = g_side[dev];
+  if (s.stream == nullptr) {
+    cudaStream_t st = nullptr;
+    if ((e = cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking)) != cudaSuccess)
+      return cuda_fail(e, "side stream / event creation");
+    s.stream = st;
+  }
+  *out = &s;
+  return ICSA_OK;
+}
+
+// side waits for the work enqueued on `stream` so far
+int fork_to(const SideStream* s, cudaStream_t stream) {
+  cudaError_t e = cudaEventRecord(s->fork, stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s->stream, s->fork, 0);
+  return e == cudaSuccess ? ICSA_OK : cuda_fail(e, "fork to the side stream");
+}
+
+// `stream` waits for the work enqueued on the side stream so far
+int join_from(const SideStream* s, cudaStream_t stream) {
+  cudaError_t e = cudaEventRecord(s->join, s->stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, s->join, 0);
+  return e == cudaSuccess ? ICSA_OK : cuda_fail(e, "join from the side stream");
+}
+
 icsa::SelectParams make_select_params(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, const void* k,
                                       const void* v) {
   icsa::SelectParams s;
@@ -226,11 +280,12 @@ int run_pool(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, co
   return e == cudaSuccess ? ICSA_OK : cuda_fail(e, "pool");
 }
 
-int run_select(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, const void* k, const void* v,
-               cudaStream_t stream) {
-  icsa::SelectParams s = make_select_params(p, L, ws, k, v);
-  cudaError_t e = icsa::launch_compressed_attention(s, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "compressed attention");
+// The selection chain after the row statistics (column sums, the two sorts,
+// the extended KV and the per-block top-k), on `stream`.
+int run_selection_chain(const icsa_problem* p, const icsa_workspace_layout& L, const icsa::SelectParams& s,
+                        cudaStream_t stream) {
+  cudaError_t e = icsa::launch_colsum(s, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "column sums");
   e = icsa::launch_selection(s, stream);
   if (e != cudaSuccess) return cuda_fail(e, "block selection");
   e = icsa::launch_extended_kv(s, stream);
@@ -249,6 +304,24 @@ int run_select(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, 
   e = icsa::launch_sparse_topk(s, stream);
   if (e != cudaSuccess) return cuda_fail(e, "sparse top-k");
   return ICSA_OK;
+}
+
+int run_select(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, const void* k, const void* v,
+               cudaStream_t stream) {
+  icsa::SelectParams s = make_select_params(p, L, ws, k, v);
+  cudaError_t e = icsa::launch_compressed_scores(s, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "compressed scores");
+  // out_compress is read only by the attention epilogue: it runs on the side
+  // stream beside the selection chain
+  std::lock_guard<std::mutex> lock(g_side_mutex);
+  SideStream* side = nullptr;
+  int rc = side_stream(&side);
+  if (rc == ICSA_OK) rc = fork_to(side, stream);
+  if (rc != ICSA_OK) return rc;
+  e = icsa::launch_outc(s, side->stream);
+  rc = e == cudaSuccess ? run_selection_chain(p, L, s, stream) : cuda_fail(e, "out_compress");
+  const int jrc = join_from(side, stream);
+  return rc != ICSA_OK ? rc : jrc;
 }
 
 constexpr int kAttendDense = 1, kAttendSparse = 2;
@@ -293,6 +366,22 @@ int run_attend(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, 
     a.out_tma = 1;
   }
   a.err = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + L.err);
+  if (parts == (kAttendDense | kAttendSparse) && p->num_flat > 0 && L.n_sparse > 0) {
+    // both halves: the dense attention is launched first on the caller's
+    // stream and the block-sparse attention on the side stream, so the
+    // sparse CTAs fill the SMs that the dense kernel's last wave leaves idle
+    std::lock_guard<std::mutex> lock(g_side_mutex);
+    SideStream* side = nullptr;
+    if ((rc = side_stream(&side)) != ICSA_OK || (rc = fork_to(side, stream)) != ICSA_OK) return rc;
+    cudaError_t e = icsa::launch_flat_attention(a, maps, p->D, stream);
+    rc = e == cudaSuccess ? ICSA_OK : cuda_fail(e, "dense attention");
+    if (rc == ICSA_OK) {
+      e = icsa::launch_sparse_attention(a, maps, p->D, side->stream);
+      if (e != cudaSuccess) rc = cuda_fail(e, "sparse attention");
+    }
+    const int jrc = join_from(side, stream);
+    return rc != ICSA_OK ? rc : jrc;
+  }
   if (parts & kAttendDense) {
     cudaError_t e = icsa::launch_flat_attention(a, maps, p->D, stream);
     if (e != cudaSuccess) return cuda_fail(e, "dense attention");

@@ -63,7 +63,12 @@ struct SelectParams {
   __nv_bfloat16* newv;
 };
 
-cudaError_t launch_compressed_attention(const SelectParams& p, cudaStream_t stream);
+// Compressed attention: scores, row statistics and in-context column sums on
+// `stream`; out_compress (which only the attention epilogue reads) on
+// `outc_stream`, which the caller orders after the row statistics.
+cudaError_t launch_compressed_scores(const SelectParams& p, cudaStream_t stream);
+cudaError_t launch_outc(const SelectParams& p, cudaStream_t stream);
+cudaError_t launch_colsum(const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_selection(const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_extended_kv(const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_sparse_topk(const SelectParams& p, cudaStream_t stream);

@@ -250,7 +250,7 @@ __global__ void colsum_kernel(SelectParams p) {
 
 }  // namespace
 
-cudaError_t launch_compressed_attention(const SelectParams& p, cudaStream_t stream) {
+cudaError_t launch_compressed_scores(const SelectParams& p, cudaStream_t stream) {
   const int BH = p.B * p.H;
   dim3 g1((p.NB + kGT - 1) / kGT, (p.NB + kGT - 1) / kGT, BH);
   scores_kernel<<<g1, 256, 0, stream>>>(p);
@@ -269,22 +269,22 @@ cudaError_t launch_compressed_attention(const SelectParams& p, cudaStream_t stre
   }
   dim3 g2((p.NB + warps - 1) / warps, BH);
   rowstats_kernel<<<g2, warps * 32, smem, stream>>>(p, warps, stride);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
 
-  dim3 g3((p.NB + kOR - 1) / kOR, BH);
+cudaError_t launch_outc(const SelectParams& p, cudaStream_t stream) {
+  dim3 g3((p.NB + kOR - 1) / kOR, p.B * p.H);
   if (p.D == 128) outc_kernel<128><<<g3, 256, 0, stream>>>(p);
   else if (p.D == 64) outc_kernel<64><<<g3, 256, 0, stream>>>(p);
   else return cudaErrorInvalidValue;
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
 
-  if (p.n_s > 0) {
-    dim3 g4((p.n_s + 31) / 32, BH);
-    colsum_kernel<<<g4, dim3(32, 8), 0, stream>>>(p);
-    e = cudaGetLastError();
-  }
-  return e;
+cudaError_t launch_colsum(const SelectParams& p, cudaStream_t stream) {
+  if (p.n_s <= 0) return cudaSuccess;
+  dim3 g4((p.n_s + 31) / 32, p.B * p.H);
+  colsum_kernel<<<g4, dim3(32, 8), 0, stream>>>(p);
+  return cudaGetLastError();
 }
 
 }  // namespace icsa

@@ -190,6 +190,51 @@ def test_stage_entry_points_equal_forward(cuda_device):
     assert torch.equal(out1, out2)
 
 
+def test_call_is_ordered_on_the_callers_stream(cuda_device):
+    """Part of the call runs on the library's own second stream (out_compress,
+    and the block-sparse attention beside the dense one); the caller's stream
+    still waits for all of it: a copy enqueued on the same non-default stream
+    right after each call sees the finished output."""
+    from in_context_sparse_attention import editing_sparse_attention
+    B, S, H, D, t = 1, 16384, 8, 128, 8192
+    q, k, v = (x.cuda() for x in _rand(B, S, H, D, torch.bfloat16, seed=51, t=t))
+    want = run_gpu(q, k, v, t)[0]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    snaps = []
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            snaps.append(editing_sparse_attention(q, k, v, t, S - t).clone())
+    torch.cuda.synchronize()
+    for snap in snaps:
+        assert torch.equal(snap, want)
+
+
+def test_graph_capture_replays_the_call(cuda_device):
+    """The call captured into a CUDA graph (side-stream work included, by its
+    fork and join events) replays to the eager result, and to the eager
+    result of new inputs written into the captured input buffers."""
+    from in_context_sparse_attention import editing_sparse_attention
+    B, S, H, D, t = 1, 8192, 4, 128, 4096
+    q, k, v = (x.cuda() for x in _rand(B, S, H, D, torch.bfloat16, seed=61, t=t))
+    want = run_gpu(q, k, v, t)[0]  # eager first: the library creates its side stream outside the capture
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = editing_sparse_attention(q, k, v, t, S - t)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    q2, k2, v2 = (x.cuda() for x in _rand(B, S, H, D, torch.bfloat16, seed=62, t=t))
+    want2 = run_gpu(q2, k2, v2, t)[0]
+    q.copy_(q2)
+    k.copy_(k2)
+    v.copy_(v2)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, want2)
+    del g
+
+
 @pytest.mark.parametrize("group_heads", [None, 1, 3])
 def test_host_streaming_equals_device_call(cuda_device, group_heads):
     """Pinned host inputs streamed by head groups give the same bytes as the
