@@ -51,16 +51,20 @@ __global__ void __launch_bounds__(256) scores_kernel(SelectParams p) {
   const float* A = p.qmean + size_t(bh) * p.NB * p.D;
   const float* Bm = p.kmean + size_t(bh) * p.NB * p.D;
   const int lr = threadIdx.x >> 1, lk = (threadIdx.x & 1) * 4;  // loader: row, first k of a float4
+  const bool ra = i0 + lr < p.NB, rb = j0 + lr < p.NB;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  // the next k-chunk is loaded into registers while the current one is used
+  float4 va = ra ? *reinterpret_cast<const float4*>(A + size_t(i0 + lr) * p.D + lk) : z4;
+  float4 vb = rb ? *reinterpret_cast<const float4*>(Bm + size_t(j0 + lr) * p.D + lk) : z4;
   float acc[8][8] = {};
   for (int k0 = 0; k0 < p.D; k0 += kGK) {
-    {
-      const float4 za = make_float4(0.f, 0.f, 0.f, 0.f);
-      const float4 va = (i0 + lr < p.NB) ? *reinterpret_cast<const float4*>(A + size_t(i0 + lr) * p.D + k0 + lk) : za;
-      const float4 vb = (j0 + lr < p.NB) ? *reinterpret_cast<const float4*>(Bm + size_t(j0 + lr) * p.D + k0 + lk) : za;
-      As[lk + 0][lr] = va.x; As[lk + 1][lr] = va.y; As[lk + 2][lr] = va.z; As[lk + 3][lr] = va.w;
-      Bs[lk + 0][lr] = vb.x; Bs[lk + 1][lr] = vb.y; Bs[lk + 2][lr] = vb.z; Bs[lk + 3][lr] = vb.w;
-    }
+    As[lk + 0][lr] = va.x; As[lk + 1][lr] = va.y; As[lk + 2][lr] = va.z; As[lk + 3][lr] = va.w;
+    Bs[lk + 0][lr] = vb.x; Bs[lk + 1][lr] = vb.y; Bs[lk + 2][lr] = vb.z; Bs[lk + 3][lr] = vb.w;
     __syncthreads();
+    if (k0 + kGK < p.D) {
+      va = ra ? *reinterpret_cast<const float4*>(A + size_t(i0 + lr) * p.D + k0 + kGK + lk) : z4;
+      vb = rb ? *reinterpret_cast<const float4*>(Bm + size_t(j0 + lr) * p.D + k0 + kGK + lk) : z4;
+    }
 #pragma unroll
     for (int c = 0; c < kGK; ++c) {
       const float4 a0 = *reinterpret_cast<const float4*>(&As[c][ty * 4]);
@@ -172,24 +176,44 @@ __global__ void __launch_bounds__(256) outc_kernel(SelectParams p) {
   }
   __syncthreads();
   const int pr = threadIdx.x >> 2, pc = (threadIdx.x & 3) * 8;  // P loader: row, first of 8 columns
+  constexpr int kVL = kOJ * D / 4 / 256;                          // float4 of V per thread and chunk
+  const int i = i0 + pr;
+  // the scores and V rows of the next chunk are loaded into registers while
+  // the current chunk is used
+  float sraw[8];
+  float4 vr[kVL];
+  auto fetch = [&](int j0) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int j = j0 + pc + e;
+      sraw[e] = (i < p.NB && j < p.NB) ? S[size_t(i) * p.NB + j] : 0.f;
+    }
+#pragma unroll
+    for (int t = 0; t < kVL; ++t) {
+      const int e = threadIdx.x + t * 256;
+      const int jr = e / (D / 4), dc = (e % (D / 4)) * 4;
+      vr[t] = (j0 + jr < p.NB) ? *reinterpret_cast<const float4*>(V + size_t(j0 + jr) * D + dc)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
   float acc[4][kCW] = {};
+  fetch(0);
   for (int j0 = 0; j0 < p.NB; j0 += kOJ) {
     {
-      const int i = i0 + pr;
       const float m = sm[pr], il = sl[pr];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int j = j0 + pc + e;
-        Ps[pc + e][pr] = (i < p.NB && j < p.NB) ? fast_exp2(fmaf(S[size_t(i) * p.NB + j], kLog2e, -m)) * il : 0.f;
+        Ps[pc + e][pr] = (i < p.NB && j < p.NB) ? fast_exp2(fmaf(sraw[e], kLog2e, -m)) * il : 0.f;
       }
     }
-    for (int e = threadIdx.x; e < kOJ * D / 4; e += 256) {
-      const int jr = e / (D / 4), dc = (e % (D / 4)) * 4;
-      const float4 v = (j0 + jr < p.NB) ? *reinterpret_cast<const float4*>(V + size_t(j0 + jr) * D + dc)
-                                        : make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<float4*>(&Vs[jr][dc]) = v;
+#pragma unroll
+    for (int t = 0; t < kVL; ++t) {
+      const int e = threadIdx.x + t * 256;
+      *reinterpret_cast<float4*>(&Vs[e / (D / 4)][(e % (D / 4)) * 4]) = vr[t];
     }
     __syncthreads();
+    if (j0 + kOJ < p.NB) fetch(j0 + kOJ);
 #pragma unroll 8
     for (int c = 0; c < kOJ; ++c) {
       const float4 a = *reinterpret_cast<const float4*>(&Ps[c][ty * 4]);
