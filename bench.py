@@ -224,47 +224,29 @@ class Runner:
 _CPU_INPUTS = {}
 
 
-def cpu_reference_sample(w, head_count=1, chunk=64, seed_base=0):
-    """Run the CPU restatement of the whole call for the first `head_count`
-    heads of workload `w` (every stage, every query block, in chunks of
-    `chunk` blocks) and scale to all heads.  Returns (ms/call, seconds spent,
-    description)."""
+def cpu_reference_sample(w, head_count=2, seed_base=0):
+    """Run the CPU restatement of the whole call (oracle.icsa_oracle.
+    editing_sparse_attention: the reference's orchestration,
+    editing_sparse_attention.py:67-232, with the TileLang kernel and
+    flash_attn_func restated; pinned bit for bit against the reference's own
+    orchestrator on configuration 1) for the first `head_count` heads of
+    workload `w` at its full sequence length, and scale to all heads (every
+    stage is independent per head).  The dense part runs in fp32, flash-attn's
+    accumulation type.  Returns (ms/call, seconds spent, description)."""
     from oracle import icsa_oracle as orc
     torch.set_num_threads(os.cpu_count() or 1)
-    t = w.t_seq_len
-    c = orc.Counts.make(w.B, w.S, 1, w.D, t)
-    spent = 0.0
-    for h in range(head_count):
-        key = (w.name, h, seed_base)
-        if key not in _CPU_INPUTS:
-            _CPU_INPUTS[key] = tuple(x.float() for x in synthetic.make_inputs(w, heads=[h], seed_base=seed_base,
-                                                                              device="cpu"))
-        q, k, v = _CPU_INPUTS[key]
-        t0 = time.perf_counter()
-        qm, km, vm = orc.block_means(q), orc.block_means(k), orc.block_means(v)
-        s, P, out_c = orc.compressed_attention(*(x.to(torch.bfloat16).permute(0, 2, 1, 3) for x in (qm, km, vm)))
-        sel = orc.select_desc(orc.incontext_keys(P, c.n_t), c.topK)
-        order = orc.select_desc(orc.sharpness_keys(P, c.n_t, c.k_sparsity), c.NB)
-        nk = orc.extended_kv(k, t, sel)[0, 0].to(torch.bfloat16)
-        nv = orc.extended_kv(v, t, sel)[0, 0].to(torch.bfloat16)
-        qb = q[0, :, 0].to(torch.bfloat16).view(c.NB, 64, w.D)
-        kc = orc.block_sums_bf16(nk[None, :, None])[0, 0]
-        vc = orc.block_sums_bf16(nv[None, :, None])[0, 0]
-        nkf, nvf = nk.float(), nv.float()
-        for i in range(0, c.num_flat, chunk):
-            fb = order[0, 0, i:min(c.num_flat, i + chunk)]
-            qf = qb[fb].reshape(-1, w.D).float()
-            sc = torch.softmax((qf @ nkf.t()) / (w.D ** 0.5), dim=-1)
-            _ = (sc @ nvf).to(torch.bfloat16)
-        for i in range(c.num_flat, c.NB, chunk):
-            sb = order[0, 0, i:min(c.NB, i + chunk)]
-            qsum = orc.block_sums_bf16(qb[sb].reshape(1, -1, 1, w.D))[0, 0]
-            idx = orc.select_desc(qsum.float() @ kc.float().t(), c.top_k)
-            _ = orc.sparse_kernel(qb[sb], nk, nv, kc, vc, idx, c.nkv)
-        spent += time.perf_counter() - t0
-    desc = (f"the whole call for {head_count} of {w.H} heads (pooling, compressed attention, selections, "
-            f"extended KV, all {c.num_flat} flat and {c.n_sparse} sparse query blocks), scaled to {w.H} heads; "
-            f"fp32 torch on {torch.get_num_threads()} threads")
+    key = (w.name, head_count, seed_base)
+    if key not in _CPU_INPUTS:
+        _CPU_INPUTS[key] = synthetic.make_inputs(w, heads=range(head_count), seed_base=seed_base, device="cpu")
+    q, k, v = _CPU_INPUTS[key]
+    t0 = time.perf_counter()
+    r = orc.editing_sparse_attention(q, k, v, w.t_seq_len, dense_dtype=torch.float32)
+    spent = time.perf_counter() - t0
+    c = r.counts
+    desc = (f"the whole call for {head_count} of {w.H} heads at the full sequence length (pooling, compressed "
+            f"attention, selections, extended KV, all {c.num_flat} flat and {c.n_sparse} sparse query blocks), "
+            f"scaled x{w.H / head_count:g} to {w.H} heads; the oracle's restatement of the reference orchestration "
+            f"(torch, fp32 dense part) on {torch.get_num_threads()} threads")
     return spent / head_count * w.H * 1e3, spent, desc
 
 
@@ -279,17 +261,24 @@ def run_reference_arm(args, rank):
                           "is hours of host time"}), flush=True)
         return
     w = WORKLOADS[args.workload]
+    heads = min(args.ref_heads, w.H)
     for _ in range(args.warmup):
-        cpu_reference_sample(w)
-    vals = []
+        cpu_reference_sample(w, head_count=heads)
+    vals, secs = [], []
     for _ in range(args.steps):
-        ms, _, desc = cpu_reference_sample(w)
+        ms, sec, desc = cpu_reference_sample(w, head_count=heads)
         vals.append(ms)
+        secs.append(sec)
     value = statistics.mean(vals)
+    # a timed step is the bounded sample (heads of the call); `value` is the
+    # whole call, scaled from it
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "ms/call", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": value, "higher_is_better": False,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": config_dict(w, args.gpus),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(secs) * 1e3,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded blurred-field generator)", "config": config_dict(w, args.gpus),
+            "extrapolation": {"heads_per_step": heads, "heads_per_call": w.H, "factor": w.H / heads,
+                              "note": "ms_per_step is the measured time of one step (the sample); value is "
+                                      "ms_per_step scaled to all heads of one call"},
             "cpu_baseline": {"value": value, "unit": "ms/call", "cores": torch.get_num_threads(), "kind": "port",
                              "sample": desc},
             "e2e": {"value": value, "unit": "ms/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -505,6 +494,111 @@ def run_sweep(args, local):
                       "gpu_launches": launches, "rows": rows}), flush=True)
 
 
+class NumaLocal:
+    """Within the block, the calling thread runs on the CPUs of the NUMA node
+    the GPU hangs off (sysfs local_cpulist of its PCI function), so pinned
+    host buffers allocated and first touched there live in that node's
+    memory.  The previous affinity is restored on exit; `node` is the CPU
+    list used, or None when it could not be read or binding is disabled."""
+
+    def __init__(self, dev, enabled=True):
+        self.dev, self.enabled, self.saved, self.node = dev, enabled, None, None
+
+    def __enter__(self):
+        if not self.enabled or not hasattr(os, "sched_setaffinity"):
+            return self
+        try:
+            pr = torch.cuda.get_device_properties(self.dev)
+            bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            with open(f"/sys/bus/pci/devices/{bus}/local_cpulist") as f:
+                text = f.read().strip()
+            cpus = set()
+            for part in text.split(","):
+                a, _, b = part.partition("-")
+                cpus.update(range(int(a), int(b or a) + 1))
+            self.saved = os.sched_getaffinity(0)
+            cpus &= self.saved
+            if cpus and cpus != self.saved:
+                os.sched_setaffinity(0, cpus)
+                self.node = text
+            elif cpus:
+                self.node = f"{text} (every CPU this process may use is local)"
+        except Exception:  # noqa: BLE001
+            self.node = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.saved is not None:
+            os.sched_setaffinity(0, self.saved)
+        return False
+
+
+def measure_link(host_in, host_out, dev, barrier, reps=3):
+    """Pinned host <-> device copy rates of this rank (GB/s), with every rank
+    copying at the same time (barrier before each direction): plain
+    contiguous copies of the same byte counts as one e2e step."""
+    dins = [torch.empty_like(h, device=dev) for h in host_in]
+    dout = torch.empty_like(host_out, device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    rates = []
+    for direction in ("h2d", "d2h"):
+        pairs = list(zip(dins, host_in)) if direction == "h2d" else [(host_out, dout)]
+        nbytes = sum(h.numel() * h.element_size() for _, h in pairs)
+        for dst, src in pairs:  # one untimed pass
+            dst.copy_(src, non_blocking=True)
+        barrier()
+        e0.record()
+        for _ in range(reps):
+            for dst, src in pairs:
+                dst.copy_(src, non_blocking=True)
+        e1.record()
+        barrier()
+        rates.append(reps * nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+    del dins, dout
+    return rates[0], rates[1]
+
+
+def time_reference_dense(q, k, v, num_flat, tkv, steps):
+    """The reference's dense part on this GPU: flash_attn_func (the library
+    call of editing_sparse_attention.py:211-215, flash-attn 2.8 as installed
+    in this image) on the flat half's shapes -- num_flat*64 queries against
+    the tkv rows of the extended KV -- timed with CUDA events; torch SDPA is
+    timed beside it.  It is the 93 % of the reference call's FLOPs that a
+    library already does on the GPU, so it bounds the reference's GPU time
+    from below.  Query rows and KV rows are slices of q, k and v: the work
+    depends only on the shapes."""
+    import torch.nn.functional as F
+    qf = q[:, :num_flat * 64].contiguous()
+    kf, vf = k[:, :tkv].contiguous(), v[:, :tkv].contiguous()
+    res = {"shape": {"q": list(qf.shape), "kv": list(kf.shape)}}
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / steps
+
+    try:
+        import flash_attn
+        from flash_attn import flash_attn_func
+        res["flash_attn_ms"] = timed(lambda: flash_attn_func(qf, kf, vf))
+        res["flash_attn_version"] = flash_attn.__version__
+    except Exception as e:  # noqa: BLE001
+        res["flash_attn_unavailable"] = f"{type(e).__name__}: {str(e)[:200]}"
+    try:
+        qt, kt, vt = (x.transpose(1, 2) for x in (qf, kf, vf))
+        res["torch_sdpa_ms"] = timed(lambda: F.scaled_dot_product_attention(qt, kt, vt))
+    except Exception as e:  # noqa: BLE001
+        res["torch_sdpa_unavailable"] = f"{type(e).__name__}: {str(e)[:200]}"
+    return res
+
+
 def config_dict(w, n):
     return {"workload": w.name, "B": w.B, "H": w.H, "D": w.D, "S": w.S, "t_seq_len": w.t_seq_len,
             "grid": list(w.grid), "heads_per_gpu": w.H // n, "parallelism": f"head-sharded x{n}",
@@ -530,7 +624,12 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--cpu-heads", type=int, default=8, help="heads the CPU baseline runs in full")
+    ap.add_argument("--cpu-heads", type=int, default=4, help="heads the CPU baseline runs in full")
+    ap.add_argument("--ref-heads", type=int, default=2, help="heads per step of --impl reference")
+    ap.add_argument("--no-numa-bind", action="store_true",
+                    help="e2e: do not place the pinned host buffers on the GPU's NUMA node")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's dense-part library (flash-attn) on this GPU")
     ap.add_argument("--heads", type=int, default=0, help="run only this many heads (profiling of a small case)")
     args = ap.parse_args()
 
@@ -606,8 +705,10 @@ def main():
     # timed region
     e2e = None
     if not args.no_e2e:
-        hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
-        hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+        with NumaLocal(dev, enabled=not args.no_numa_bind) as numa:
+            hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+            hout = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+            hout.zero_()
 
         def e2e_step():
             editing_sparse_attention(hq, hk, hv, w.t_seq_len, w.t_seq_len, out=hout, non_blocking=True)
@@ -625,16 +726,39 @@ def main():
         e2e = {"value": e2e_ms, "unit": "ms/call", "path": "editing_sparse_attention on pinned host tensors",
                "h2d_bytes_per_step": 3 * q.numel() * q.element_size() * world,
                "d2h_bytes_per_step": q.numel() * q.element_size() * world}
+        # the host link's rates with every rank copying at once, and the floor
+        # they put under e2e: the slower direction of this rank's bytes
+        h2d_gbs, d2h_gbs = measure_link((hq, hk, hv), hout, dev, barrier)
+        rank_in, rank_out = 3 * q.numel() * q.element_size(), q.numel() * q.element_size()
+        floor = max(rank_in / (h2d_gbs * 1e9), rank_out / (d2h_gbs * 1e9)) * 1e3
+        link = [h2d_gbs, d2h_gbs, floor]
+        if dist is not None:
+            gathered = [torch.zeros(3, device=dev) for _ in range(world)]
+            dist.all_gather(gathered, torch.tensor(link, device=dev))
+            link = torch.stack(gathered).cpu().tolist()
+        else:
+            link = [link]
+        e2e["link"] = {"h2d_gbs_per_rank": [r[0] for r in link], "d2h_gbs_per_rank": [r[1] for r in link],
+                       "floor_ms": max(r[2] for r in link),
+                       "measured": "pinned contiguous copies of each rank's step bytes, all ranks at once",
+                       "numa_bound_cpus": numa.node}
 
     ms = elapsed / args.steps
+    # time x clock of this rank (the power cap moves the clock with the load)
+    ms_x_mhz = ms * (clk["sm_mhz"] or 0.0)
     if dist is not None:
         names = sorted(stage)
-        t = torch.tensor([ms, e2e["value"] if e2e else 0.0] + [stage[n] for n in names], device=dev)
+        t = torch.tensor([ms, e2e["value"] if e2e else 0.0, ms_x_mhz] + [stage[n] for n in names], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
         if e2e:
             e2e["value"] = float(t[1])
-        stage = {n: float(x) for n, x in zip(names, t[2:])}
+        ms_x_mhz = float(t[2])
+        stage = {n: float(x) for n, x in zip(names, t[3:])}
+        mhz = torch.zeros(world, device=dev)
+        mhz[rank] = clk["sm_mhz"] or 0.0
+        dist.all_reduce(mhz)
+        clk["sm_mhz_per_rank"] = mhz.cpu().tolist()
     sustained, burst, hbm, src = peaks()
     _, flops, sparse_flops = attention_flops(runner.p, runner.L.n_sparse)
     # dominant kernel: the dense attention of the flat query blocks (one launch per call)
@@ -662,8 +786,20 @@ def main():
                              "sparse_kernel": {"achieved": sparse_achieved, "frac": sparse_achieved / sustained,
                                                "flops_per_launch": sparse_flops}},
                 "clocks": clk, "gpu_launches": KERNELS_PER_CALL_ALIGNED * args.steps}
+        if ms_x_mhz and clk.get("sm_max_mhz"):
+            line["clock_normalised"] = {
+                "ms_x_mhz": ms_x_mhz, "ms_at_sm_max_mhz": ms_x_mhz / clk["sm_max_mhz"],
+                "note": "max over ranks of (ms per call x median SM MHz under load); compare across N to factor "
+                        "out the power cap's clock"}
         if e2e:
             line["e2e"] = e2e
+        if world == 1 and not args.no_reference_gpu:
+            line["reference_gpu"] = time_reference_dense(q, k, v, runner.p.num_flat, runner.p.tkv,
+                                                         max(3, args.steps // 2))
+            line["reference_gpu"]["note"] = (
+                "the reference's dense part alone (flash_attn_func, 93% of the call's FLOPs) on this GPU; its "
+                "TileLang/Triton kernels are JIT-compiled from the reference's sources, which this repository "
+                "does not carry to the GPU box")
         if world == 1 and not args.no_cpu_baseline:
             cms, secs, desc = cpu_reference_sample(w, head_count=args.cpu_heads)
             line["cpu_baseline"] = {"value": cms, "unit": "ms/call", "cores": torch.get_num_threads(),

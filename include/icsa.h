@@ -14,11 +14,15 @@
  *   - Every call is asynchronous on `stream` and performs no host
  *     synchronisation; it can be captured into a CUDA graph.
  *   - icsa_select and icsa_attend (and so icsa_forward) run part of their
- *     kernels on a second stream of the library's own, forked from `stream`
+ *     kernels on a side stream of the library's own, forked from `stream`
  *     and joined back to it by events: work enqueued on `stream` after the
- *     call still runs after all of it.  The library creates that stream and
- *     its two events on the first such call on each device; make that first
- *     call before any stream capture.
+ *     call still runs after all of it.  Each device has a small pool of such
+ *     side streams: calls on different caller streams use different ones,
+ *     and a side stream that has joined a stream capture serves only calls
+ *     of that capture until it ends, so eager calls on other streams (or
+ *     other captures) may run while a capture is open.  The library creates
+ *     the first side streams on the first such call on each device; make that
+ *     first call before any stream capture.
  *   - Every function returns an icsa_status; on failure
  *     icsa_last_error() returns a message for the calling thread.
  *   - Scratch memory ("workspace") is provided by the caller; its size comes
@@ -216,6 +220,20 @@ ICSA_API int icsa_forward_host(const icsa_problem* p, int group_heads, const voi
 ICSA_API int icsa_device_status(void* workspace, cudaStream_t stream);
 
 /*
+ * Per-device record of device-side timeouts, for callers that no longer hold
+ * the workspace of the calls they made (no counterpart in the reference,
+ * whose host asserts and raises: tilelang_host.py:251-260,
+ * editing_sparse_attention.py:31-34).  Every bounded wait that gives up also
+ * writes its code into a status word of the current device that outlives the
+ * call.  This function synchronises `stream`, then returns ICSA_OK if no wait
+ * on the current device gave up since the record was last cleared, else
+ * ICSA_ERR_DEVICE_TIMEOUT (with the code in icsa_last_error()).  With
+ * `clear` != 0 it clears the record.  It synchronises, so it cannot be
+ * captured in a CUDA graph; call it after a graph replay instead.
+ */
+ICSA_API int icsa_last_status(cudaStream_t stream, int clear);
+
+/*
  * Self-test of the device-side bounded waits (no counterpart in the
  * reference): launches a kernel whose mbarrier wait can never complete; the
  * wait gives up after about one second, records a status code in the first
@@ -238,6 +256,8 @@ ICSA_API int icsa_wait_selftest(void* workspace, cudaStream_t stream);
  * All calls share that one array: calls that overlap on the GPU race, so
  * order them on one stream.  The first call on each device looks the array's
  * address up (and may load the module); make it before any stream capture.
+ * The address is kept per CUDA context: after a cudaDeviceReset() the next
+ * call looks it up again in the new context.
  * No cudaMalloc/cudaFree or other allocating routine is called.
  */
 ICSA_API int icsa_forward_static(const icsa_problem* p, const void* q, const void* k, const void* v,
@@ -245,6 +265,14 @@ ICSA_API int icsa_forward_static(const icsa_problem* p, const void* q, const voi
 
 /* Size in bytes of the static scratch used by icsa_forward_static. */
 ICSA_API size_t icsa_static_scratch_bytes(void);
+
+/*
+ * icsa_device_status for the static scratch of icsa_forward_static: waits
+ * for `stream` and returns ICSA_OK, or ICSA_ERR_DEVICE_TIMEOUT if a
+ * device-side bounded wait of the preceding icsa_forward_static calls on the
+ * current device gave up.  Like icsa_forward_static it allocates nothing.
+ */
+ICSA_API int icsa_static_device_status(cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -184,41 +184,105 @@ int check_call(const icsa_problem* p, void* ws, size_t ws_bytes, icsa_workspace_
 }
 
 // ---------------------------------------------------------------------------
-// A second stream per device for the parts of one call that may run side by
-// side: out_compress beside the selection chain, and the block-sparse
-// attention beside the dense attention (its CTAs take the SMs that the dense
-// kernel's last wave leaves idle).  Side work is ordered by events: the side
-// stream waits for an event recorded on the caller's stream, and the caller's
-// stream waits for an event recorded after the side work, so the caller sees
-// one ordered call and a captured caller stream captures the side work too.
-// The stream and events are created by the first call on a device.  The
-// mutex keeps host threads from interleaving their use of the two events.
+// Side streams for the parts of one call that may run side by side:
+// out_compress beside the selection chain, and the block-sparse attention
+// beside the dense attention (its CTAs take the SMs that the dense kernel's
+// last wave leaves idle).  Side work is ordered by events: the side stream
+// waits for an event recorded on the caller's stream, and the caller's stream
+// waits for an event recorded after the side work, so the caller sees one
+// ordered call and a captured caller stream captures the side work too.
+//
+// Each device has a small pool of side streams (each with its own two
+// events).  A call takes the side stream that last served its caller stream
+// when that one is free for it, else the least recently used free one:
+// * a side stream that has joined a stream capture stays inside it until the
+//   capture ends, so while a capture is open it serves only calls of that
+//   same capture; eager calls, and other captures, take another one;
+// * eager calls on different caller streams get different side streams (up
+//   to kMaxSides per device), so they are not serialised behind each other.
+// kPrecreated side streams are created by the first call on a device; more
+// are created on demand, which a call inside a capture cannot always do
+// (stream creation is refused in some capture modes), hence the first call
+// on a device belongs outside any capture.  The mutex keeps host threads from
+// interleaving their use of one side stream's events.
 // ---------------------------------------------------------------------------
 constexpr int kMaxDevices = 64;
+constexpr int kPrecreated = 2, kMaxSides = 8;
 
 struct SideStream {
   cudaStream_t stream = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
+  cudaStream_t owner = nullptr;  // caller stream it served last
+  uint64_t last_use = 0;
+};
+struct DeviceSides {
+  SideStream pool[kMaxSides];
+  int count = 0;
+  uint64_t tick = 0;
 };
 std::mutex g_side_mutex;
-SideStream g_side[kMaxDevices];
+DeviceSides g_side[kMaxDevices];
 
-// Called with g_side_mutex held.
-int side_stream(SideStream** out) {
+int create_side(SideStream* s) {
+  cudaError_t e;
+  if ((e = cudaEventCreateWithFlags(&s->fork, cudaEventDisableTiming)) != cudaSuccess ||
+      (e = cudaEventCreateWithFlags(&s->join, cudaEventDisableTiming)) != cudaSuccess ||
+      (e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking)) != cudaSuccess)
+    return cuda_fail(e, "side stream / event creation (make the first call on a device outside stream capture)");
+  return ICSA_OK;
+}
+
+// Capture state of a stream: 0 idle, 1 inside capture `*id`, -1 inside an
+// invalidated capture (busy until that capture ends).
+int capture_state(cudaStream_t s, unsigned long long* id) {
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  *id = 0;
+  if (cudaStreamGetCaptureInfo(s, &st, id) != cudaSuccess) return -1;
+  return st == cudaStreamCaptureStatusNone ? 0 : st == cudaStreamCaptureStatusActive ? 1 : -1;
+}
+
+// Called with g_side_mutex held: a side stream for work forked from `caller`.
+int side_stream(cudaStream_t caller, SideStream** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(ICSA_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
-  SideStream& s = g_side[dev];
-  if (s.stream == nullptr) {
-    cudaStream_t st = nullptr;
-    if ((e = cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming)) != cudaSuccess ||
-        (e = cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming)) != cudaSuccess ||
-        (e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking)) != cudaSuccess)
-      return cuda_fail(e, "side stream / event creation");
-    s.stream = st;
+  DeviceSides& d = g_side[dev];
+  while (d.count < kPrecreated) {
+    const int rc = create_side(&d.pool[d.count]);
+    if (rc != ICSA_OK) return rc;
+    ++d.count;
   }
-  *out = &s;
+  unsigned long long cid = 0;
+  const int cstate = capture_state(caller, &cid);
+  if (cstate < 0) return fail(ICSA_ERR_CUDA, "the caller's stream is inside an invalidated stream capture");
+  // usable: idle, or already inside the caller's own capture
+  auto usable = [&](SideStream& s) {
+    unsigned long long sid = 0;
+    const int st = capture_state(s.stream, &sid);
+    return st == 0 || (st == 1 && cstate == 1 && sid == cid);
+  };
+  SideStream* pick = nullptr;
+  for (int i = 0; i < d.count && pick == nullptr; ++i)
+    if (d.pool[i].owner == caller && usable(d.pool[i])) pick = &d.pool[i];
+  if (pick == nullptr) {
+    // a side stream no other caller has claimed yet, else the least recently used usable one
+    for (int i = 0; i < d.count && pick == nullptr; ++i)
+      if (d.pool[i].owner == nullptr && usable(d.pool[i])) pick = &d.pool[i];
+    if (pick == nullptr && d.count < kMaxSides) {
+      const int rc = create_side(&d.pool[d.count]);
+      if (rc != ICSA_OK) return rc;
+      pick = &d.pool[d.count++];
+    }
+    if (pick == nullptr)
+      for (int i = 0; i < d.count; ++i)
+        if (usable(d.pool[i]) && (pick == nullptr || d.pool[i].last_use < pick->last_use)) pick = &d.pool[i];
+  }
+  if (pick == nullptr)
+    return fail(ICSA_ERR_UNSUPPORTED, "all %d side streams of device %d are inside other stream captures", d.count, dev);
+  pick->owner = caller;
+  pick->last_use = ++d.tick;
+  *out = pick;
   return ICSA_OK;
 }
 
@@ -315,7 +379,7 @@ int run_select(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, 
   // stream beside the selection chain
   std::lock_guard<std::mutex> lock(g_side_mutex);
   SideStream* side = nullptr;
-  int rc = side_stream(&side);
+  int rc = side_stream(stream, &side);
   if (rc == ICSA_OK) rc = fork_to(side, stream);
   if (rc != ICSA_OK) return rc;
   e = icsa::launch_outc(s, side->stream);
@@ -372,7 +436,7 @@ int run_attend(const icsa_problem* p, const icsa_workspace_layout& L, void* ws, 
     // sparse CTAs fill the SMs that the dense kernel's last wave leaves idle
     std::lock_guard<std::mutex> lock(g_side_mutex);
     SideStream* side = nullptr;
-    if ((rc = side_stream(&side)) != ICSA_OK || (rc = fork_to(side, stream)) != ICSA_OK) return rc;
+    if ((rc = side_stream(stream, &side)) != ICSA_OK || (rc = fork_to(side, stream)) != ICSA_OK) return rc;
     cudaError_t e = icsa::launch_flat_attention(a, maps, p->D, stream);
     rc = e == cudaSuccess ? ICSA_OK : cuda_fail(e, "dense attention");
     if (rc == ICSA_OK) {
@@ -516,6 +580,39 @@ int icsa_device_status(void* workspace, cudaStream_t stream) {
   e = cudaMemcpy(&code, workspace, sizeof(int), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "status read");
   if (code != 0) return fail(ICSA_ERR_DEVICE_TIMEOUT, "a device-side wait gave up (code 0x%x)", code);
+  return ICSA_OK;
+}
+
+int icsa_last_status(cudaStream_t stream, int clear) {
+  constexpr int kUnits = 4;
+  static std::mutex mu;
+  static int* addr[kMaxDevices][kUnits] = {};
+  cudaError_t e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(ICSA_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev][0] == nullptr) {
+    cudaError_t (*const get[kUnits])(int**) = {icsa::sticky_status_dense_pair, icsa::sticky_status_flat,
+                                               icsa::sticky_status_sparse, icsa::sticky_status_selftest};
+    int* a[kUnits] = {};
+    for (int i = 0; i < kUnits; ++i)
+      if ((e = get[i](&a[i])) != cudaSuccess) return cuda_fail(e, "sticky status address");
+    for (int i = 0; i < kUnits; ++i) addr[dev][i] = a[i];
+  }
+  int first = 0;
+  for (int i = 0; i < kUnits; ++i) {
+    int code = 0;
+    if ((e = cudaMemcpy(&code, addr[dev][i], sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+      return cuda_fail(e, "sticky status read");
+    if (code != 0 && first == 0) first = code;
+    if (code != 0 && clear && (e = cudaMemset(addr[dev][i], 0, sizeof(int))) != cudaSuccess)
+      return cuda_fail(e, "sticky status clear");
+  }
+  if (first != 0)
+    return fail(ICSA_ERR_DEVICE_TIMEOUT, "a device-side wait on device %d gave up since the last check (code 0x%x)",
+                dev, first);
   return ICSA_OK;
 }
 

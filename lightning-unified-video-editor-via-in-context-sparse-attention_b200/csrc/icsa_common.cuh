@@ -21,11 +21,28 @@ constexpr int kTileRows = 128;      // Q rows per attention tile (two 64-token b
 
 // ---------------------------------------------------------------------------
 // Error reporting from device code.  Every bounded wait that gives up writes a
-// code here (first writer wins) and the kernel winds down instead of hanging.
+// code into the call's status word `err` (first writer wins) and the kernel
+// winds down instead of hanging.
+//
+// The same code also goes into g_sticky_status, a per-device record that
+// outlives the call's workspace: icsa_last_status() reads (and clears) it, so
+// a caller that has discarded the workspace still learns that a wait gave up.
+// The variable is file-scope static, so every translation unit that includes
+// this header has its own copy; the units whose kernels wait define an
+// accessor with ICSA_DEFINE_STICKY_ACCESSOR and icsa_capi.cu reads them all.
 // ---------------------------------------------------------------------------
+static __device__ int g_sticky_status;
+
 ICSA_DEV void report_error(int* err, int code) {
   if (err != nullptr) atomicCAS(err, 0, code);
+  atomicCAS(&g_sticky_status, 0, code);
 }
+
+// Host accessor of this translation unit's copy of g_sticky_status.
+#define ICSA_DEFINE_STICKY_ACCESSOR(fn)                                    \
+  cudaError_t fn(int** out) {                                              \
+    return cudaGetSymbolAddress(reinterpret_cast<void**>(out), g_sticky_status); \
+  }
 
 // ---------------------------------------------------------------------------
 // bf16 helpers

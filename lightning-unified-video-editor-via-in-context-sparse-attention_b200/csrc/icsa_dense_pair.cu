@@ -513,4 +513,6 @@ cudaError_t launch_dense_pair_attention(const AttnParams& p, const AttnMaps& map
   return cudaGetLastError();
 }
 
+ICSA_DEFINE_STICKY_ACCESSOR(sticky_status_dense_pair)
+
 }  // namespace icsa

@@ -396,4 +396,6 @@ cudaError_t launch_flat_attention(const AttnParams& p, const AttnMaps& maps, int
   return cudaGetLastError();
 }
 
+ICSA_DEFINE_STICKY_ACCESSOR(sticky_status_flat)
+
 }  // namespace icsa

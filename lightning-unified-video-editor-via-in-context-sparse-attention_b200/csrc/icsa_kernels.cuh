@@ -114,4 +114,11 @@ cudaError_t launch_dense_pair_attention(const AttnParams& p, const AttnMaps& map
 // Block-sparse tiles (exact top_k blocks + interval term), P kept in TMEM.
 cudaError_t launch_sparse_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
 
+// Device addresses of the per-device sticky status words of the translation
+// units whose kernels have bounded waits (see report_error).
+cudaError_t sticky_status_dense_pair(int** out);
+cudaError_t sticky_status_flat(int** out);
+cudaError_t sticky_status_sparse(int** out);
+cudaError_t sticky_status_selftest(int** out);
+
 }  // namespace icsa

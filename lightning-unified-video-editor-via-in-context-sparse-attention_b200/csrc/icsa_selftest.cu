@@ -27,6 +27,10 @@ __global__ void wait_selftest_kernel(int* status) {
 
 }  // namespace
 
+namespace icsa {
+ICSA_DEFINE_STICKY_ACCESSOR(sticky_status_selftest)
+}  // namespace icsa
+
 extern "C" ICSA_API int icsa_wait_selftest(void* workspace, cudaStream_t stream) {
   if (workspace == nullptr) {
     icsa_set_last_error("workspace is NULL");

@@ -581,4 +581,6 @@ cudaError_t launch_sparse_attention(const AttnParams& p, const AttnMaps& maps, i
   return cudaGetLastError();
 }
 
+ICSA_DEFINE_STICKY_ACCESSOR(sticky_status_sparse)
+
 }  // namespace icsa

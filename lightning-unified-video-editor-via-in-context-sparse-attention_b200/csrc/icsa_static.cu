@@ -22,7 +22,12 @@
 //     the device status word, is cleared by every call;
 //   * the first call on each device resolves the array's device address
 //     (cudaGetSymbolAddress, which may load the module).  Make that first call
-//     outside any stream capture.
+//     outside any stream capture.  The address belongs to the CUDA context:
+//     it is cached with the context's unique id (cuCtxGetId), so after a
+//     cudaDeviceReset() the first call in the new context resolves it again;
+//   * icsa_static_device_status() reads the scratch's device status word, so
+//     a device-side wait that gave up in one of these calls is reported even
+//     though the caller never sees the scratch.
 #include <cstdio>
 #include <mutex>
 
@@ -39,9 +44,36 @@ static __device__ __align__(256) unsigned char g_icsa_static_scratch[kIcsaStatic
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
 void* g_scratch_ptr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};  // cuCtxGetId of the context the address belongs to
 
-// Resolves (once per device, with that device current) the device address of
-// the scratch array.
+// Unique id of the calling thread's current context (0 if it cannot be read).
+// The driver entry points are fetched through the runtime, so the library
+// does not link against libcuda.
+unsigned long long current_context_id() {
+  typedef CUresult (*GetCurrentFn)(CUcontext*);
+  typedef CUresult (*GetIdFn)(CUcontext, unsigned long long*);
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  if (get_current == nullptr || get_id == nullptr) {
+    void* a = nullptr;
+    void* b = nullptr;
+    cudaDriverEntryPointQueryResult qa, qb;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &a, cudaEnableDefault, &qa) != cudaSuccess ||
+        qa != cudaDriverEntryPointSuccess ||
+        cudaGetDriverEntryPoint("cuCtxGetId", &b, cudaEnableDefault, &qb) != cudaSuccess ||
+        qb != cudaDriverEntryPointSuccess)
+      return 0;
+    get_current = reinterpret_cast<GetCurrentFn>(a);
+    get_id = reinterpret_cast<GetIdFn>(b);
+  }
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Resolves (once per device and context, with that device current) the
+// device address of the scratch array.
 int icsa_static_scratch_resolve(void** out, char* msg, size_t msg_len) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -54,7 +86,10 @@ int icsa_static_scratch_resolve(void** out, char* msg, size_t msg_len) {
     return ICSA_ERR_UNSUPPORTED;
   }
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
+  // a context exists once the runtime has been used on this device; before
+  // that the id reads 0 and the lookup below creates the primary context
+  const unsigned long long ctx = current_context_id();
+  if (g_scratch_ptr[dev] == nullptr || ctx == 0 || ctx != g_scratch_ctx[dev]) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_icsa_static_scratch);
     if (e != cudaSuccess || ptr == nullptr) {
@@ -62,6 +97,7 @@ int icsa_static_scratch_resolve(void** out, char* msg, size_t msg_len) {
       return ICSA_ERR_CUDA;
     }
     g_scratch_ptr[dev] = ptr;
+    g_scratch_ctx[dev] = current_context_id();
   }
   *out = g_scratch_ptr[dev];
   return ICSA_OK;
@@ -92,4 +128,15 @@ extern "C" ICSA_API int icsa_forward_static(const icsa_problem* p, const void* q
     return rc;
   }
   return icsa_forward(p, q, k, v, alpha, out, scratch, kIcsaStaticScratchBytes, stream);
+}
+
+extern "C" ICSA_API int icsa_static_device_status(cudaStream_t stream) {
+  void* scratch = nullptr;
+  char msg[256];
+  const int rc = icsa_static_scratch_resolve(&scratch, msg, sizeof(msg));
+  if (rc != ICSA_OK) {
+    icsa_set_last_error(msg);
+    return rc;
+  }
+  return icsa_device_status(scratch, stream);
 }

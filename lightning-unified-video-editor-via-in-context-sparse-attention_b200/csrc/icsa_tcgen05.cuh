@@ -167,6 +167,24 @@ ICSA_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
       : "memory");
 }
 
+// 16 consecutive columns
+ICSA_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : ICSA_R8(0), ICSA_R8(8)
+      : "r"(taddr)
+      : "memory");
+}
+
+ICSA_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      ICSA_W8(0), ICSA_W8(8)
+      : "memory");
+}
+
 #undef ICSA_R8
 #undef ICSA_W8
 

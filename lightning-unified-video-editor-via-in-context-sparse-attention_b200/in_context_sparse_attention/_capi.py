@@ -21,7 +21,8 @@ STATUS = {0: "ICSA_OK", 1: "ICSA_ERR_INVALID", 2: "ICSA_ERR_UNSUPPORTED", 3: "IC
 EXPORTED = ("icsa_last_error", "icsa_version", "icsa_problem_init", "icsa_workspace_size",
             "icsa_get_workspace_layout", "icsa_forward", "icsa_pool", "icsa_select", "icsa_attend",
             "icsa_attend_dense", "icsa_attend_sparse", "icsa_host_workspace_size", "icsa_forward_host", "icsa_wait_selftest",
-            "icsa_device_status")
+            "icsa_device_status", "icsa_last_status", "icsa_forward_static", "icsa_static_scratch_bytes",
+            "icsa_static_device_status")
 
 
 class Problem(ctypes.Structure):
@@ -102,6 +103,14 @@ def load(path: str = None) -> ctypes.CDLL:
         lib.icsa_wait_selftest.restype = i
         lib.icsa_device_status.argtypes = [vp, vp]
         lib.icsa_device_status.restype = i
+        lib.icsa_last_status.argtypes = [vp, i]
+        lib.icsa_last_status.restype = i
+        lib.icsa_forward_static.argtypes = [pp, vp, vp, vp, vp, vp, vp]
+        lib.icsa_forward_static.restype = i
+        lib.icsa_static_scratch_bytes.argtypes = []
+        lib.icsa_static_scratch_bytes.restype = sz
+        lib.icsa_static_device_status.argtypes = [vp]
+        lib.icsa_static_device_status.restype = i
         _lib = lib
         return lib
 

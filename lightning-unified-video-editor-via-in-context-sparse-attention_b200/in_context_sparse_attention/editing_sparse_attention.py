@@ -34,17 +34,53 @@ workspace from the PyTorch caching allocator, so it can be captured in a CUDA
 graph.  With pinned CPU inputs it returns once the result is in host memory,
 unless ``non_blocking=True`` (then synchronise the current stream before
 reading the result); ``out=`` takes a preallocated pinned result tensor.
+
+Device-side timeouts.  Every wait inside the kernels is bounded (about one
+second); a wait that gives up records a status code instead of hanging, and
+the kernel returns with an unfinished result.  The reference raises on
+failure (its host asserts, tilelang_host.py:251-260), so this package raises
+IcsaError (a RuntimeError) when such a code is found:
+* pinned CPU inputs with ``non_blocking=False``: always, after the result has
+  reached host memory;
+* CUDA inputs: with ``check=True`` (or the environment variable
+  ICSA_CHECK_STATUS=1), which synchronises the stream after the call; the
+  check is skipped while the stream is being captured into a CUDA graph;
+* otherwise: ``device_status()``, which synchronises and reports a wait that
+  gave up in any call on the device since the last check.
 """
 from __future__ import annotations
 
 import ctypes
 import numbers
+import os
 
 import torch
 
 from . import _capi
 
 BLOCK_M = 64
+_CHECK_DEFAULT = os.environ.get("ICSA_CHECK_STATUS", "0") not in ("", "0")
+
+
+def _check_status(lib, ws_ptr, stream_handle, where):
+    """Synchronises `stream_handle` and raises IcsaError if a device-side
+    wait gave up: the per-device record (icsa_last_status, cleared by this
+    check) covers every call on the device since the last check, the
+    workspace status word `ws_ptr` (when given) this call."""
+    rc = lib.icsa_last_status(stream_handle, 1)
+    _capi.check(rc, where)
+    if ws_ptr:
+        _capi.check(lib.icsa_device_status(ws_ptr, stream_handle), where)
+
+
+def device_status(device=None):
+    """Synchronises the current stream of `device` (default: the current
+    CUDA device) and raises IcsaError if a device-side wait of any call on
+    that device gave up since the last check; clears the record."""
+    lib = _capi.load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        _check_status(lib, None, torch.cuda.current_stream(dev).cuda_stream, "device_status")
 
 
 class Backend:
@@ -162,17 +198,18 @@ def _streamed(lib, p, q, k, v, alpha_t, out_dt, out, group_heads, non_blocking):
         _capi.check(rc, "icsa_forward_host")
         ws.record_stream(stream)
         if not non_blocking:
-            stream.synchronize()
+            _check_status(lib, ws.data_ptr(), stream.cuda_stream, "editing_sparse_attention (pinned host)")
     return out
 
 
 def editing_sparse_attention(q, k, v, t_seq_len, s_seq_len=None, alpha_2=1.0, alpha_3=1.0, SPARSITY_RATIO=0.0625,
                              backend=Backend.B200, *, select_ratio=0.125, flat_ratio=0.5, out=None,
-                             group_heads=None, non_blocking=False, _debug=None):
+                             group_heads=None, non_blocking=False, check=None, _debug=None):
     """In-context sparse attention (see the module docstring).  Returns x
     [B, S, H, D].  `out`, `group_heads` and `non_blocking` apply to pinned
-    CPU inputs only.  `_debug`, when a dict, receives the workspace and its
-    layout (used by the parity tests to read selections and keys)."""
+    CPU inputs only; `check` (default: ICSA_CHECK_STATUS) to CUDA inputs.
+    `_debug`, when a dict, receives the workspace and its layout (used by the
+    parity tests to read selections and keys)."""
     Backend.validate(backend)
     lib = _capi.load()
     p, out_dt, alpha_t = _prepare(q, k, v, t_seq_len, alpha_2, SPARSITY_RATIO, select_ratio, flat_ratio,
@@ -200,6 +237,8 @@ def editing_sparse_attention(q, k, v, t_seq_len, s_seq_len=None, alpha_2=1.0, al
                               alpha_t.data_ptr() if alpha_t is not None else None, out.data_ptr(),
                               ws.data_ptr(), size, stream)
         _capi.check(rc, "icsa_forward")
+        if (_CHECK_DEFAULT if check is None else check) and not torch.cuda.is_current_stream_capturing():
+            _check_status(lib, ws.data_ptr(), stream, "editing_sparse_attention")
     if _debug is not None:
         _debug.update(workspace=ws, layout=_capi.workspace_layout(p), problem=p, inputs=(q, k, v))
     return out

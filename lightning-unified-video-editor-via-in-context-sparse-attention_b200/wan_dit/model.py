@@ -455,13 +455,23 @@ class WanDiT:
         u = torch.einsum("bfhwpqrc->bcfphqwr", u)
         return u.reshape(B, cfg.out_dim, f * pf, h * ph, w * pw)
 
-    def denoise_step(self, latent, source_latent, t, sigma, sigma_next, context, seq_len, guidance_scale=2.5):
+    def denoise_step(self, latent, source_latent, t, sigma, sigma_next, context, seq_len, guidance_scale=2.5,
+                     check_status=True):
         """One denoising step of the reference's loop (inference.py:266-291):
         both CFG branches in one batch (context[0] unconditional, context[1]
         conditional), noise = uncond + g * (cond - uncond), then a
         flow-matching Euler update latent + (sigma_next - sigma) * noise,
         which stands in for the reference's UniPC solver (a few elementwise
-        ops on the latent)."""
+        ops on the latent).
+
+        check_status: after the step, synchronise and raise IcsaError if a
+        bounded wait inside any attention kernel of the step gave up (the
+        per-device record of icsa_last_status); skipped while the stream is
+        being captured into a CUDA graph."""
         out = self.forward(latent, source_latent, t, context, seq_len)
         noise = out[0] + guidance_scale * (out[1] - out[0])
-        return latent + (sigma_next - sigma) * noise
+        new = latent + (sigma_next - sigma) * noise
+        if check_status and not torch.cuda.is_current_stream_capturing():
+            from in_context_sparse_attention import device_status
+            device_status(new.device)
+        return new

@@ -252,14 +252,21 @@ def sparse_backend(q_sharp, new_k, new_v, sparsity, forced_idx=None, return_keys
     return out
 
 
-def dense_attention(q, k, v):
+def dense_attention(q, k, v, dtype=torch.float64, chunk=1024):
     """flash_attn_func(q, k, v) restated: [B,T,H,D] bf16 -> exact softmax
-    attention (fp64 arithmetic), returned as bf16 values in fp32."""
-    D = q.shape[-1]
-    qd, kd, vd = (t.double().permute(0, 2, 1, 3) for t in (q, k, v))
-    s = torch.matmul(qd, kd.transpose(-1, -2)) / math.sqrt(D)
-    o = torch.matmul(torch.softmax(s, dim=-1), vd)
-    return o.permute(0, 2, 1, 3).to(torch.bfloat16).float()
+    attention in `dtype` arithmetic (fp64 for parity checks), returned as bf16
+    values in fp32.  Queries are taken `chunk` at a time, so the score matrix
+    held at once is chunk x Tkv per (b, h) whatever the sequence length."""
+    B, T, H, D = q.shape
+    out = torch.empty(B, H, T, D, dtype=torch.float32)
+    for b in range(B):
+        for h in range(H):
+            qd, kd, vd = (t[b, :, h].to(dtype).contiguous() for t in (q, k, v))
+            kt = kd.t().contiguous()
+            for i in range(0, T, chunk):
+                s = torch.matmul(qd[i:i + chunk], kt) / math.sqrt(D)
+                out[b, h, i:i + chunk] = torch.matmul(torch.softmax(s, dim=-1), vd).to(torch.bfloat16).float()
+    return out.permute(0, 2, 1, 3)
 
 
 # ---------------------------------------------------------------------------
@@ -292,14 +299,19 @@ def result_dtypes(q_dtype, k_dtype, v_dtype, alpha):
 
 
 def editing_sparse_attention(q, k, v, t_seq_len, alpha_2=1.0, sparsity=0.0625, select_ratio=0.125,
-                             flat_ratio=0.5, forced=None, means=None) -> OracleResult:
+                             flat_ratio=0.5, forced=None, means=None, dense_dtype=torch.float64) -> OracleResult:
     """The whole call on the CPU.  forced: optional dict with 'sel', 'order',
     'sparse_idx' from another implementation; when given, those selections are
     used instead of the oracle's own (so outputs can be compared without
     near-tie selection differences).  means: optional (qm, km) [B, NB, H, D]
     block means of the float32 q and k that the given bf16 q and k were
     rounded from (a sequence-parallel caller pools before it exchanges the
-    bf16 tensors); they replace the means of q and k."""
+    bf16 tensors); they replace the means of q and k.  dense_dtype: the
+    arithmetic of the dense (flash_attn_func) part; fp64 for parity checks,
+    fp32 (flash-attn's accumulation type) when the call is timed.  Memory is
+    bounded at any sequence length: the dense part takes its queries in
+    chunks, and every other stage holds at most [NB, NB] or [n_sparse, 64,
+    64] scores per (b, h)."""
     B, S, H, D = q.shape
     c = Counts.make(B, S, H, D, t_seq_len, sparsity, select_ratio, flat_ratio)
     outc_dt, ca_dt, out_dt = result_dtypes(q.dtype, k.dtype, v.dtype, alpha_2)
@@ -343,7 +355,7 @@ def editing_sparse_attention(q, k, v, t_seq_len, alpha_2=1.0, sparsity=0.0625, s
     if c.num_flat > 0:
         qf = gather(flat_blocks).reshape(B, H, c.num_flat * BLOCK, D)
         o_f = dense_attention(qf.permute(0, 2, 1, 3).to(torch.bfloat16), new_k.permute(0, 2, 1, 3).to(torch.bfloat16),
-                              new_v.permute(0, 2, 1, 3).to(torch.bfloat16))
+                              new_v.permute(0, 2, 1, 3).to(torch.bfloat16), dtype=dense_dtype)
         o_f = o_f.permute(0, 2, 1, 3).reshape(B, H, c.num_flat, BLOCK, D)
         for b in range(B):
             for h in range(H):

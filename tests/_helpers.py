@@ -1,5 +1,8 @@
 """Shared helpers of the parity tests: run the C-ABI path with its workspace
 kept, read named workspace regions, and compare with the CPU oracle."""
+import json
+import os
+
 import torch
 
 from in_context_sparse_attention import editing_sparse_attention
@@ -43,6 +46,15 @@ def gpu_selections(dbg):
                 outc=outc)
 
 
+def record(name, **fields):
+    """Appends one JSON line of measured errors to the file named by the
+    ICSA_PARITY_LOG environment variable (pytest -q hides prints)."""
+    path = os.environ.get("ICSA_PARITY_LOG")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps({"case": name, **fields}) + "\n")
+
+
 def oracle_forced(q, k, v, t_seq_len, sels, alpha=1.0, **kw):
     """Oracle output with the GPU's selections forced."""
     a = alpha.cpu() if isinstance(alpha, torch.Tensor) else alpha
@@ -53,3 +65,25 @@ def oracle_forced(q, k, v, t_seq_len, sels, alpha=1.0, **kw):
 def errors(a, b):
     d = (a.double().cpu() - b.double().cpu()).abs()
     return float(d.max()), float(d.mean())
+
+
+def bf16_ulp(x):
+    """Spacing of bf16 numbers at |x| (8 significant bits): 2^(e - 7) for
+    2^e <= |x| < 2^(e+1)."""
+    e = torch.floor(torch.log2(x.double().abs().clamp_min(2.0 ** -126)))
+    return torch.exp2(e - 7)
+
+
+def excess_over_bf16_bound(out, ref, max_abs):
+    """Largest amount by which |out - ref| exceeds max(max_abs, two bf16 units
+    of ref), and the reference value there.  Both sides are rounded to bf16
+    twice, as the reference rounds them: the attention output, then
+    x = attention + out_compress * alpha_2.  Where the two fp32 accumulations
+    straddle a rounding boundary, each rounding can move the result by one
+    unit, so two units of |x| is the smallest element-wise bound; it exceeds
+    2e-2 only for |x| >= 2 (one unit is 2^-6 there)."""
+    o, r = out.double().cpu(), ref.double().cpu()
+    d = (o - r).abs()
+    ex = d - torch.clamp(2 * bf16_ulp(r), min=max_abs)
+    i = int(torch.argmax(ex))
+    return float(ex.flatten()[i]), float(r.flatten()[i]), float(d.flatten()[i])

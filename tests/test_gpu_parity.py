@@ -11,7 +11,7 @@ import torch
 from in_context_sparse_attention import synthetic
 from oracle import icsa_oracle as orc
 
-from _helpers import errors, gpu_selections, oracle_forced, region, run_gpu
+from _helpers import errors, excess_over_bf16_bound, gpu_selections, oracle_forced, record, region, run_gpu
 
 pytestmark = pytest.mark.gpu
 
@@ -67,6 +67,7 @@ def test_call_matches_oracle(cuda_device, name):
     ref = oracle_forced(q, k, v, t, sels, flat_ratio=fr)
     mx, mn = errors(out, ref.out)
     print(f"{name}: max|d|={mx:.3e} mean|d|={mn:.3e}")
+    record(name, max_abs=mx, mean_abs=mn, dtype=str(dt))
     assert mx <= MAX_ABS_BF16 and mn <= MEAN_ABS_BF16
 
 
@@ -105,9 +106,19 @@ def test_pool_stage(cuda_device):
             torch.testing.assert_close(m, m_ref, rtol=2 ** -7 if dt == torch.bfloat16 else 1e-5, atol=1e-5)
 
 
+MEAN_ABS_F32 = 1e-4  # the fp32 tolerance of the contract, applied to the mean
+
+
 def test_golden_config1(cuda_device):
     """BASELINE configuration 1 (fp32) against the reference run recorded in
-    tests/golden/config1_reference.pt."""
+    tests/golden/config1_reference.pt.
+
+    The fp32 tolerance (1e-4) is asserted on the mean absolute error.  The
+    max-abs bound stays the bf16 one: the reference itself rounds the output
+    of both attention kernels to bf16 (editing_sparse_attention.py:187,
+    212-214), so where the GPU's fp32 accumulation lands on the other side of
+    a bf16 rounding boundary the two differ by one bf16 unit (2^-8 relative,
+    about 4e-3 at |x| ~ 1) whatever the precision of the rest."""
     import os
     fx = torch.load(os.path.join(os.path.dirname(__file__), "golden", "config1_reference.pt"))
     w = synthetic.CONFIG1
@@ -122,7 +133,8 @@ def test_golden_config1(cuda_device):
     assert torch.equal(flat_gpu, flat_ref)
     mx, mn = errors(out[:, ::13], fx["out_rows"])
     print(f"config1 vs reference: max|d|={mx:.3e} mean|d|={mn:.3e}")
-    assert mx <= MAX_ABS_BF16 and mn <= MEAN_ABS_BF16
+    record("config1_fp32_vs_reference", max_abs=mx, mean_abs=mn, dtype="torch.float32")
+    assert mx <= MAX_ABS_BF16 and mn <= MEAN_ABS_F32
 
 
 def test_alpha_tensor_mixed_dtypes(cuda_device):
@@ -261,12 +273,44 @@ def test_unpinned_host_tensors_are_refused(cuda_device):
         editing_sparse_attention(q, q, q, 64, 64)
 
 
+@pytest.mark.parametrize("workload", ["480p", "720p"])
+def test_headline_shape_output_matches_oracle(cuda_device, workload):
+    """BASELINE configurations 2 and 3 at their full sequence lengths (joint
+    65,536 and 151,296 tokens) on 2 of the 40 heads: every selection equals
+    the oracle selector applied to the GPU's own fp32 keys, and the whole
+    output matches the CPU oracle run with the GPU's selections: mean-abs
+    <= 1e-3, and max-abs <= 2e-2 wherever two bf16 units of the output are
+    below 2e-2 (|x| < 2).  Both sides round to bf16 twice (the attention, then
+    the residual sum), so where an fp32 accumulation straddles a rounding
+    boundary they differ by whole units; up to two units are admitted above
+    |x| = 2.  The oracle's dense part runs here in fp32
+    (exact softmax, chunked over queries), whose error is orders of magnitude
+    below the tolerance; the fp64 form is used at the small shapes."""
+    w = {"480p": synthetic.WAN480P, "720p": synthetic.WAN720P}[workload]
+    q, k, v = synthetic.make_inputs(w, heads=[0, 1], device="cuda")
+    out, dbg = run_gpu(q, k, v, w.t_seq_len)
+    c = orc.Counts.make(w.B, w.S, 2, w.D, w.t_seq_len)
+    sels = gpu_selections(dbg)
+    _check_selection_exact(sels, c)
+    ref = oracle_forced(q, k, v, w.t_seq_len, sels, dense_dtype=torch.float32)
+    mx, mn = errors(out, ref.out)
+    ex, at_ref, at_d = excess_over_bf16_bound(out, ref.out, MAX_ABS_BF16)
+    over = int(((out.double().cpu() - ref.out.double()).abs() > MAX_ABS_BF16).sum())
+    print(f"{w.name} (2 heads): max|d|={mx:.3e} mean|d|={mn:.3e}")
+    record(w.name + "_2heads", max_abs=mx, mean_abs=mn, dtype=str(out.dtype), worst_ref_value=at_ref,
+           worst_abs_diff=at_d, excess_over_bound=ex, elements_over_max_abs=over, elements=out.numel())
+    assert mn <= MEAN_ABS_BF16
+    # max-abs 2e-2, except that where |ref| >= 2 two bf16 units (2^-5 or more)
+    # are admitted: see the docstring
+    assert ex <= 0.0, f"|d|={at_d} at ref={at_ref}"
+
+
 def test_720p_shape_properties(cuda_device):
     """BASELINE configuration 3 shape (joint 151,296 tokens, 2364 blocks,
-    nkv 1329) on 2 heads: too large for the CPU oracle's attention, so the
-    checks are size-independent -- every selection equals the oracle selector
-    applied to the GPU's own keys, the output is finite, a repeat call gives
-    the same bytes, and the staged entry points agree with it."""
+    nkv 1329) on 2 heads, size-independent properties: every selection
+    equals the oracle selector applied to the GPU's own keys, the output is
+    finite and a repeat call gives the same bytes (the output itself is
+    compared with the oracle in test_headline_shape_output_matches_oracle)."""
     w = synthetic.WAN720P
     q, k, v = synthetic.make_inputs(w, heads=[0, 1], device="cuda")
     out, dbg = run_gpu(q, k, v, w.t_seq_len)

@@ -14,8 +14,45 @@ esa_mod = importlib.import_module("in_context_sparse_attention.editing_sparse_at
 
 
 def test_exports_mirror_the_reference_package():
-    assert set(ica.__all__) == {"Backend", "editing_sparse_attention", "editing_sparse_attention_tilelang"}
+    reference = {"Backend", "editing_sparse_attention", "editing_sparse_attention_tilelang"}
+    # plus the timeout reporting of this build (no counterpart in the reference)
+    assert set(ica.__all__) == reference | {"IcsaError", "device_status"}
     assert ica.editing_sparse_attention_tilelang is ica.editing_sparse_attention
+
+
+class _FakeLib:
+    """Stands in for libicsa.so: returns fixed status codes (no GPU)."""
+
+    def __init__(self, sticky, word):
+        self.sticky, self.word, self.calls = sticky, word, []
+
+    def icsa_last_status(self, stream, clear):
+        self.calls.append(("last", stream, clear))
+        return self.sticky
+
+    def icsa_device_status(self, ws, stream):
+        self.calls.append(("word", ws, stream))
+        return self.word
+
+    def icsa_last_error(self):
+        return b"a device-side wait gave up (code 0x102)"
+
+
+@pytest.mark.parametrize("sticky,word", [(5, 0), (0, 5)])
+def test_status_check_raises_on_a_recorded_timeout(monkeypatch, sticky, word):
+    fake = _FakeLib(sticky, word)
+    monkeypatch.setattr(ica._capi, "load", lambda path=None: fake)
+    with pytest.raises(ica.IcsaError) as e:
+        esa_mod._check_status(fake, 1234, 7, "call")
+    assert e.value.code == 5 and "ICSA_ERR_DEVICE_TIMEOUT" in str(e.value)
+    assert fake.calls[0] == ("last", 7, 1)  # the per-device record is read and cleared first
+
+
+def test_status_check_passes_when_clean(monkeypatch):
+    fake = _FakeLib(0, 0)
+    monkeypatch.setattr(ica._capi, "load", lambda path=None: fake)
+    esa_mod._check_status(fake, 1234, 7, "call")
+    assert fake.calls == [("last", 7, 1), ("word", 1234, 7)]
 
 
 def test_signature_keeps_the_reference_parameters():
