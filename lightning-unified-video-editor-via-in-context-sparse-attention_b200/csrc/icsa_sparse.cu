@@ -55,11 +55,11 @@ struct __align__(1024) SSmem {
   uint8_t k[SCfg<D>::kStages][SCfg<D>::kOpBytes];
   uint8_t v[SCfg<D>::kStages][SCfg<D>::kOpBytes];
   uint64_t q_full;
-  uint64_t k_full[SCfg<D>::kStages], k_empty[SCfg<D>::kStages];
+  uint64_t k_full[SCfg<D>::kStages];
   uint64_t v_full[SCfg<D>::kStages], v_empty[SCfg<D>::kStages];
   float outc[2][D];                       // out_compress rows of the tile's two query blocks
   uint32_t mask[2][kSMaskWords];          // their selection bit masks (when nkv_pad <= 32 * kSMaskWords)
-  uint64_t s_full[2], p_full[2], pv_done;  // p_full per S buffer: the softmax may run one step ahead
+  uint64_t s_full[2], p_full[2];          // p_full per S buffer: the softmax may run one step ahead
   uint64_t mma_fin;
   uint32_t tmem_base;
   int abort_flag;
@@ -116,7 +116,9 @@ ICSA_DEV void sparse_producer(const AttnParams& p, const AttnMaps& maps, const S
       r1 = rows[idx1[j]];
     }
     const int prow = (j - t.n_exact) * 128;  // interval: pooled rows
-    if (!mbar_wait(&sm.k_empty[st], ph, p.err, kErrKEmpty, abort_flag)) return;
+    // a stage is free once the P.V that read its values is done (its S,
+    // issued earlier, is done then too): one barrier frees both halves
+    if (!mbar_wait(&sm.v_empty[st], ph, p.err, kErrVEmpty, abort_flag)) return;
     mbar_arrive_expect_tx(&sm.k_full[st], C::kOpBytes);
     for (int c = 0; c < C::kChunks; ++c) {
       uint8_t* dst = sm.k[st] + c * kChunkBytes;
@@ -127,7 +129,6 @@ ICSA_DEV void sparse_producer(const AttnParams& p, const AttnMaps& maps, const S
         tma_load_3d(dst, &maps.kc, &sm.k_full[st], c * 64, prow, t.bh);
       }
     }
-    if (!mbar_wait(&sm.v_empty[st], ph, p.err, kErrVEmpty, abort_flag)) return;
     mbar_arrive_expect_tx(&sm.v_full[st], C::kOpBytes);
     for (int c = 0; c < C::kChunks; ++c) {
       uint8_t* dst = sm.v[st] + c * kChunkBytes;
@@ -183,7 +184,6 @@ ICSA_DEV void sparse_mma(const AttnParams& p, const STile& t, SSmem<D>& sm, uint
     sparse_issue_s_seq(qd, kd0 + uint64_t(st) * kStageStep, tmem + uint32_t(j & 1) * 128u,
                        std::make_integer_sequence<int, D / 16>{});
     tc::mma_commit_elect(&sm.s_full[j & 1]);
-    tc::mma_commit_elect(&sm.k_empty[st]);
     return true;
   };
   if (!issue_s(0)) return;
@@ -198,7 +198,7 @@ ICSA_DEV void sparse_mma(const AttnParams& p, const STile& t, SSmem<D>& sm, uint
     const uint32_t acc = interval ? (j > t.n_exact) : (j > 0);
     sparse_issue_pv_seq<D>(vd0 + uint64_t(st) * kStageStep, tmem + uint32_t(j & 1) * 128u,
                            tmem + (interval ? kSColG : kSColO), acc ? 1u : 0u, std::make_integer_sequence<int, 8>{});
-    tc::mma_commit_elect(&sm.pv_done);
+    // v_empty also tells the softmax that P.V(j) is done (before an O rescale)
     tc::mma_commit_elect(&sm.v_empty[st]);
   }
 }
@@ -298,7 +298,12 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
       }
       l += (a0 + a1) + (a2 + a3);
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        warp_mbar_wait(&sm.pv_done, uint32_t(j - 1) & 1u, p.err, kErrPvDone, abort_flag);
+        // P.V(j-1) done: the completion of v_empty for its stage.  S(j) is
+        // complete, so P.V(j-2) is too (the tensor core runs in issue order)
+        // and P.V(j+2), the stage's next user, cannot have run: the parity
+        // names exactly P.V(j-1).
+        warp_mbar_wait(&sm.v_empty[(j - 1) % SCfg<D>::kStages], uint32_t((j - 1) / SCfg<D>::kStages) & 1u, p.err,
+                       kErrPvDone, abort_flag);
         tc::fence_after_sync();
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -390,11 +395,9 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
   }
 
   // epilogue: (acc * f + g_acc) / (l * f + g_l), f re-bases acc and l on the final max.
-  // Wait for every MMA of the tile on the single-phase mma_fin barrier.  A
-  // parity wait on pv_done cannot express "P.V(n-1) done" here: S(j+1) is
-  // issued before P.V(j), so s_full(n-1) only implies that P.V(n-3) is done;
-  // with P.V(n-2) still in flight pv_done sits two phases back and a wait
-  // for parity (n-1)&1 would see the older phase complete and return early.
+  // Wait for every MMA of the tile on the single-phase mma_fin barrier: S(j+1)
+  // is issued before P.V(j), so s_full(n-1) only implies that P.V(n-3) is
+  // done, and P.V(n-2) and P.V(n-1) may still be running.
   warp_mbar_wait(&sm.mma_fin, 0u, p.err, kErrPvDone, abort_flag);
   tc::fence_after_sync();
   if (!staged) asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -506,7 +509,6 @@ __global__ void __launch_bounds__(kSThreads, 1) sparse_kernel(const AttnParams p
     mbar_init(&sm.q_full, 1);
     for (int i = 0; i < C::kStages; ++i) {
       mbar_init(&sm.k_full[i], 1);
-      mbar_init(&sm.k_empty[i], 1);
       mbar_init(&sm.v_full[i], 1);
       mbar_init(&sm.v_empty[i], 1);
     }
@@ -514,7 +516,6 @@ __global__ void __launch_bounds__(kSThreads, 1) sparse_kernel(const AttnParams p
     mbar_init(&sm.s_full[1], 1);
     mbar_init(&sm.p_full[0], 4);
     mbar_init(&sm.p_full[1], 4);
-    mbar_init(&sm.pv_done, 1);
     mbar_init(&sm.mma_fin, 1);
     sm.abort_flag = 0;
     fence_mbarrier_init();
