@@ -296,7 +296,8 @@ def dit_seq_len(latent):
     the 480p latent: 32760 | 32760 | 16), so that 8 ranks hold whole blocks."""
     t = latent[1] * (latent[2] // 2) * (latent[3] // 2)
     return -(-2 * t // 512) * 512
-DIT_LAUNCHES_PER_BLOCK = 9 + 13  # 3 LayerNorm, 3 RMSNorm/RoPE, 3 residual passes + one unaligned attention call
+DIT_LAUNCHES_PER_BLOCK = 9 + 1 + 13  # 3 LayerNorm, 3 RMSNorm/RoPE, 3 residual passes, the cross-attention + one
+                                     # unaligned attention call
 
 
 def dit_step_flops(cfg, B, S, t_seq_len):

@@ -134,6 +134,26 @@ ICSA_API int icsa_dit_norm_rope_pool(const icsa_dit_norm_rope_pool_desc* desc, c
 ICSA_API int icsa_dit_gated_residual(float* x, const void* y, int64_t ldy, int rows, int C, int rows_per_batch,
                                      const float* gate, int64_t gate_batch_stride, cudaStream_t stream);
 
+/*
+ * Softmax attention of q over k, v with the default 1/sqrt(D) scale and no
+ * mask: the DiT's cross-attention over the text tokens.  Replaces the
+ * reference's flash_attention call (wanx/attention.py:18-85) made by
+ * WanT2VCrossAttention (model.py:180-188; flash-attn's kernel in the
+ * reference).  It runs the same tcgen05 dense attention kernel as the flat
+ * query blocks of icsa_forward (D = 128: SM pairs; D = 64: one SM per tile):
+ * fp32 accumulation, P rounded to bf16 for P.V, output rounded once to bf16.
+ *   q:   bf16 [B, Lq, H, D], consecutive tokens q_row_stride elements apart
+ *        (batch stride Lq * q_row_stride)
+ *   k,v: bf16 [B, Lk, H, D], row strides k_row_stride / v_row_stride (a k|v
+ *        GEMM output [B*Lk, 2*H*D] gives v at base + H*D with stride 2*H*D)
+ *   out: bf16 [B, Lq, H, D], contiguous
+ * D must be 64 or 128; row strides multiples of 8 elements and >= H*D;
+ * all buffers 16-byte aligned.  Allocates nothing.
+ */
+ICSA_API int icsa_dit_cross_attention(const void* q, int64_t q_row_stride, const void* k, int64_t k_row_stride,
+                                      const void* v, int64_t v_row_stride, void* out, int B, int Lq, int Lk, int H,
+                                      int D, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -102,9 +102,15 @@ ICSA_DEV float load_alpha(const AttnParams& p, int b, int token, int h, int d) {
 // Residual for 32 consecutive features [d0, d0+32) of one output row:
 // x = bf16(o) + out_c * alpha, with the reference's dtype rounding (attention
 // outputs are bf16; out_compress and out_compress*alpha are bf16 when the
-// reference computes them in bf16).
+// reference computes them in bf16).  oc_row == nullptr: plain attention,
+// x = bf16(o).
 ICSA_DEV void residual32(const AttnParams& p, int b, int token, int h, const float* oc_row, int d0,
                          const float (&o)[32], float (&x)[32]) {
+  if (oc_row == nullptr) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) x[e] = bf16_round(o[e]);
+    return;
+  }
 #pragma unroll
   for (int e = 0; e < 32; ++e) {
     const int d = d0 + e;

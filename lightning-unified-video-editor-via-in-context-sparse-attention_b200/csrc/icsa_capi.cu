@@ -10,6 +10,7 @@
 #include <mutex>
 
 #include "icsa_kernels.cuh"
+#include "icsa_dit.h"
 
 namespace {
 
@@ -130,12 +131,14 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// bf16 [B, rows, H, D] with a {64, 1, 64, 1} box (64 features x 64 rows).
-int encode_rows_map(CUtensorMap* m, const void* base, int B, int rows, int H, int D) {
+// bf16 [B, rows, H, D] with a {64, 1, 64, 1} box (64 features x 64 rows);
+// consecutive rows `row_stride` elements apart (H * D when contiguous).
+int encode_rows_map(CUtensorMap* m, const void* base, int B, int rows, int H, int D, int64_t row_stride = 0) {
   EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr) return fail(ICSA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const cuuint64_t rs = row_stride > 0 ? cuuint64_t(row_stride) : cuuint64_t(H) * D;
   const cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(H), cuuint64_t(rows), cuuint64_t(B)};
-  const cuuint64_t strides[3] = {cuuint64_t(D) * 2, cuuint64_t(H) * D * 2, cuuint64_t(rows) * H * D * 2};
+  const cuuint64_t strides[3] = {cuuint64_t(D) * 2, rs * 2, cuuint64_t(rows) * rs * 2};
   const cuuint32_t box[4] = {64, 1, 64, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
@@ -581,6 +584,50 @@ int icsa_device_status(void* workspace, cudaStream_t stream) {
   if (e != cudaSuccess) return cuda_fail(e, "status read");
   if (code != 0) return fail(ICSA_ERR_DEVICE_TIMEOUT, "a device-side wait gave up (code 0x%x)", code);
   return ICSA_OK;
+}
+
+int icsa_dit_cross_attention(const void* q, int64_t q_row_stride, const void* k, int64_t k_row_stride,
+                             const void* v, int64_t v_row_stride, void* out, int B, int Lq, int Lk, int H, int D,
+                             cudaStream_t stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
+    return fail(ICSA_ERR_INVALID, "cross attention: q, k, v and out must be non-NULL");
+  if (B < 1 || Lq < 1 || Lk < 1 || H < 1)
+    return fail(ICSA_ERR_INVALID, "cross attention: B, Lq, Lk, H must be positive (got %d, %d, %d, %d)", B, Lq, Lk, H);
+  if (D != 64 && D != 128) return fail(ICSA_ERR_UNSUPPORTED, "cross attention: head dim D=%d (supported: 64, 128)", D);
+  const int64_t hd = int64_t(H) * D;
+  const int64_t strides[3] = {q_row_stride, k_row_stride, v_row_stride};
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] < hd || strides[i] % 8 != 0)
+      return fail(ICSA_ERR_INVALID, "cross attention: row strides must be multiples of 8 elements and >= H*D=%lld",
+                  (long long)hd);
+  const void* ptrs[4] = {q, k, v, out};
+  for (int i = 0; i < 4; ++i)
+    if ((reinterpret_cast<uintptr_t>(ptrs[i]) & 15u) != 0)
+      return fail(ICSA_ERR_INVALID, "cross attention: buffers must be 16-byte aligned");
+  const int nbq = (Lq + icsa::kBlock - 1) / icsa::kBlock, nbk = (Lk + icsa::kBlock - 1) / icsa::kBlock;
+  if (nbq > (1 << 24) || nbk > 16384)
+    return fail(ICSA_ERR_UNSUPPORTED, "cross attention: Lq=%d / Lk=%d exceed this build's limits", Lq, Lk);
+  icsa::AttnMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  int rc;
+  if ((rc = encode_rows_map(&maps.q, q, B, Lq, H, D, q_row_stride)) != ICSA_OK) return rc;
+  if ((rc = encode_rows_map(&maps.k, k, B, Lk, H, D, k_row_stride)) != ICSA_OK) return rc;
+  if ((rc = encode_rows_map(&maps.v, v, B, Lk, H, D, v_row_stride)) != ICSA_OK) return rc;
+  if ((rc = encode_rows_map(&maps.o, out, B, Lq, H, D)) != ICSA_OK) return rc;
+  // every query block is a "flat" block in its natural order, the keys are
+  // the Lk rows of k / v (no order table, no block table), and there is no
+  // residual term: the dense attention kernels compute softmax(q k^T / sqrt(D)) v
+  icsa::AttnParams a;
+  std::memset(&a, 0, sizeof(a));
+  a.B = B; a.S = Lq; a.H = H; a.NB = nbq;
+  a.num_flat = nbq; a.n_sparse = 0;
+  a.flat_tiles = (nbq + 1) / 2; a.sparse_tiles = 0;
+  a.nkv = nbk; a.nkv_pad = (nbk + 127) / 128 * 128; a.tkv = Lk; a.top_k = 0;
+  a.scale_log2 = float(std::sqrt(1.0 / D) * 1.44269504);
+  a.alpha_mode = ICSA_ALPHA_SCALAR; a.alpha_scalar = 0.f;
+  a.out = out; a.out_dtype = ICSA_BF16; a.out_tma = 1;
+  cudaError_t e = icsa::launch_flat_attention(a, maps, D, stream);
+  return e == cudaSuccess ? ICSA_OK : cuda_fail(e, "cross attention");
 }
 
 int icsa_last_status(cudaStream_t stream, int clear) {

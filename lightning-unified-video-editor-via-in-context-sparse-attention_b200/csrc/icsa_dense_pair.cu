@@ -82,12 +82,14 @@ ICSA_DEV PTile decode_pair_tile(const AttnParams& p) {
   const int g = pr % groups;
   t.b = t.bh / p.H;
   t.h = t.bh % p.H;
-  const int* order = p.order + size_t(t.bh) * p.NB;  // flat blocks come first
+  // flat blocks come first; no order table: query block r is block r
+  const int* order = p.order ? p.order + size_t(t.bh) * p.NB : nullptr;
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int r = 4 * g + 2 * int(t.rank) + i;
     t.write[i] = r < p.num_flat;
-    t.blk[i] = order[t.write[i] ? r : p.num_flat - 1];
+    const int rr = t.write[i] ? r : p.num_flat - 1;
+    t.blk[i] = order ? order[rr] : rr;
   }
   t.n_steps = (p.nkv + 1) / 2;
   return t;
@@ -104,12 +106,13 @@ ICSA_DEV void pair_producer(const AttnParams& p, const AttnMaps& maps, const PTi
     for (int half = 0; half < 2; ++half)
       pair::tma_load_4d(sm.q + c * kChunkBytes + half * (kChunkBytes / 2), &maps.q, q_full, c * 64, t.h,
                         t.blk[half] * kBlock, t.b);
-  const int* rows = p.kv_rows + size_t(t.bh) * p.nkv;
+  // no block table: KV block i starts at row 64 i
+  const int* rows = p.kv_rows ? p.kv_rows + size_t(t.bh) * p.nkv : nullptr;
   for (int j = 0; j < t.n_steps; ++j) {
     const int s = j % kPStages;
     const uint32_t ph = uint32_t(j / kPStages) & 1u;
-    const int r0 = rows[2 * j];
-    const int r1 = (2 * j + 1 < p.nkv) ? rows[2 * j + 1] : r0;  // missing half: masked by the softmax
+    const int r0 = rows ? rows[2 * j] : 2 * j * kBlock;
+    const int r1 = (2 * j + 1 < p.nkv) ? (rows ? rows[2 * j + 1] : (2 * j + 1) * kBlock) : r0;  // missing half: masked by the softmax
     if (!mbar_wait(&sm.kv_empty[s], ph ^ 1u, p.err, kErrKEmpty, abort_flag)) return;
     if (leader) mbar_arrive_expect_tx(&sm.kv_full[s], 2 * (kPKBytes + kPVBytes));
     const uint32_t kv_full = pair::mapa(&sm.kv_full[s], 0);
@@ -223,7 +226,8 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const AttnMaps& maps, const PTil
   // feature (row & 63) + 64 w (read after the epilogue's barrier 14)
   {
     const int hb = row >> 6, d = (row & 63) + 64 * w;
-    const float cval = p.outc[(size_t(t.bh) * p.NB + (hb ? t.blk[1] : t.blk[0])) * 128 + d];
+    // no out_compress (plain attention): a zero residual term, x = bf16(o)
+    const float cval = p.outc ? p.outc[(size_t(t.bh) * p.NB + (hb ? t.blk[1] : t.blk[0])) * 128 + d] : 0.f;
     sm.ocs[hb][d] = (p.alpha_mode == ICSA_ALPHA_SCALAR) ? ca_scalar(p, cval) : cval;
   }
   const uint32_t s_free = pair::mapa(&sm.s_free[w], 0);

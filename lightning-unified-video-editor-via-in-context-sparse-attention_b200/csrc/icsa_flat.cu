@@ -71,12 +71,14 @@ ICSA_DEV FTile decode_flat_tile(const AttnParams& p, int cta) {
   const int g = cta % groups;
   t.b = t.bh / p.H;
   t.h = t.bh % p.H;
-  const int* order = p.order + size_t(t.bh) * p.NB;  // flat blocks come first
+  // flat blocks come first; no order table: query block r is block r
+  const int* order = p.order ? p.order + size_t(t.bh) * p.NB : nullptr;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int r = 4 * g + i;
     t.write[i] = r < p.num_flat;
-    t.blk[i] = order[t.write[i] ? r : p.num_flat - 1];
+    const int rr = t.write[i] ? r : p.num_flat - 1;
+    t.blk[i] = order ? order[rr] : rr;
   }
   t.n_steps = (p.nkv + 1) / 2;
   return t;
@@ -93,10 +95,11 @@ ICSA_DEV void flat_producer(const AttnParams& p, const AttnMaps& maps, const FTi
       for (int half = 0; half < 2; ++half)
         tma_load_4d(sm.q[tile] + c * kChunkBytes + half * (kChunkBytes / 2), &maps.q, &sm.q_full, c * 64, t.h,
                     t.blk[2 * tile + half] * kBlock, t.b);
-  const int* rows = p.kv_rows + size_t(t.bh) * p.nkv;
+  // no block table: KV block i starts at row 64 i
+  const int* rows = p.kv_rows ? p.kv_rows + size_t(t.bh) * p.nkv : nullptr;
   for (int j = 0; j < t.n_steps; ++j) {
-    const int r0 = rows[2 * j];
-    const int r1 = (2 * j + 1 < p.nkv) ? rows[2 * j + 1] : r0;  // missing half: masked by the softmax
+    const int r0 = rows ? rows[2 * j] : 2 * j * kBlock;
+    const int r1 = (2 * j + 1 < p.nkv) ? (rows ? rows[2 * j + 1] : (2 * j + 1) * kBlock) : r0;  // missing half: masked by the softmax
     const int ks = j % C::kKStages;
     if (!mbar_wait(&sm.k_empty[ks], (uint32_t(j / C::kKStages) & 1u) ^ 1u, p.err, kErrKEmpty, abort_flag)) return;
     mbar_arrive_expect_tx(&sm.k_full[ks], C::kOpBytes);
@@ -284,7 +287,7 @@ ICSA_DEV void flat_softmax(const AttnParams& p, const FTile& t, FSmem<D>& sm, ui
   const int token = blk * kBlock + (row & 63);
   const bool write = wr && token < p.S;
   const float inv = l == 0.f ? 0.f : 1.0f / l;
-  const float* oc = p.outc + (size_t(t.bh) * p.NB + blk) * D;
+  const float* oc = p.outc ? p.outc + (size_t(t.bh) * p.NB + blk) * D : nullptr;  // nullptr: no residual term
   const size_t out_row = ((size_t(t.b) * p.S + token) * p.H + t.h) * D;
 #pragma unroll 1
   for (int c = 0; c < D / 32; ++c) {

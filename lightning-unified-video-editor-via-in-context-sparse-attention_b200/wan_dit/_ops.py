@@ -1,12 +1,12 @@
 """Operations of one Wan 2.2 DiT block, as the model in this package calls them.
 
 `CudaOps` is the implementation: the fused elementwise passes and the
-in-context sparse attention run in libicsa.so (include/icsa_dit.h,
-include/icsa.h); the projections are library GEMMs (torch.nn.functional.linear,
-i.e. cuBLAS, bf16 in / bf16 out with f32 accumulation, which is what the
-reference's nn.Linear computes under CUDA autocast); the cross-attention over
-the 512 text tokens is torch's scaled_dot_product_attention, the library
-counterpart of the reference's flash_attention call (wanx/attention.py:18-85).
+in-context sparse attention and the cross-attention over the text tokens
+(the reference's flash_attention call, wanx/attention.py:18-85) run in
+libicsa.so (include/icsa_dit.h, include/icsa.h); the projections are library
+GEMMs (torch.nn.functional.linear, i.e. cuBLAS, bf16 in / bf16 out with f32
+accumulation, which is what the reference's nn.Linear computes under CUDA
+autocast).
 Constructing it loads libicsa.so and raises if it is missing: there is no CPU
 fallback.
 
@@ -23,7 +23,7 @@ import torch.nn.functional as F
 from in_context_sparse_attention import _capi
 
 DIT_EXPORTED = ("icsa_dit_modulated_norm", "icsa_dit_norm_rope", "icsa_dit_norm_rope_pool",
-                "icsa_dit_gated_residual")
+                "icsa_dit_gated_residual", "icsa_dit_cross_attention")
 
 _DT = {torch.bfloat16: _capi.ICSA_BF16, torch.float32: _capi.ICSA_F32}
 
@@ -73,6 +73,8 @@ def _load():
     lib.icsa_dit_norm_rope_pool.restype = i
     lib.icsa_dit_gated_residual.argtypes = [vp, vp, i64, i, i, i, vp, i64, vp]
     lib.icsa_dit_gated_residual.restype = i
+    lib.icsa_dit_cross_attention.argtypes = [vp, i64, vp, i64, vp, i64, vp, i, i, i, i, i, vp]
+    lib.icsa_dit_cross_attention.restype = i
     return lib
 
 
@@ -275,9 +277,22 @@ class CudaOps:
                     "icsa_attend")
         return out
 
-    @staticmethod
-    def cross_attention(q, k, v):
+    def cross_attention(self, q, k, v):
         """Softmax attention of bf16 q [B, L, H, D] over k, v [B, Lk, H, D]
-        with the default 1/sqrt(D) scale; bf16 [B, L, H, D]."""
-        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
-        return o.transpose(1, 2)
+        with the default 1/sqrt(D) scale; bf16 [B, L, H, D].  This library's
+        tcgen05 dense attention kernel (icsa_dit_cross_attention); each of
+        q, k, v may have any token stride (rows of a wider GEMM output) as
+        long as its heads and features are contiguous."""
+        B, L, H, D = q.shape
+        Lk = k.shape[1]
+        args = []
+        for name, t, n in (("q", q, L), ("k", k, Lk), ("v", v, Lk)):
+            if t.dtype != torch.bfloat16 or t.shape != (B, n, H, D):
+                raise ValueError(f"cross_attention: {name} must be bf16 [{B}, {n}, {H}, {D}]")
+            if t.stride(3) != 1 or t.stride(2) != D or t.stride(0) != n * t.stride(1):
+                t = t.contiguous()
+            args += [t.data_ptr(), t.stride(1)]
+        out = torch.empty(B, L, H, D, dtype=torch.bfloat16, device=q.device)
+        _capi.check(self.lib.icsa_dit_cross_attention(*args, out.data_ptr(), B, L, Lk, H, D, _stream()),
+                    "icsa_dit_cross_attention")
+        return out

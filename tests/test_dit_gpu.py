@@ -235,3 +235,36 @@ def test_pooled_qk_give_the_f32_call_bit_for_bit(ops, grid, S, t_aligned):
     out_b = ops.self_attention(qb.view(B, S, H, D), kb.view(B, S, H, D), v_b.view(B, S, H, D), alpha, t,
                                means=(qm.view(B, H, NB, D), km.view(B, H, NB, D)))
     assert torch.equal(out_a, out_b)
+
+
+@pytest.mark.parametrize("shape", [
+    # B, Lq, Lk, H, D, v taken from a k|v GEMM output (strided rows)
+    (2, 4096, 512, 4, 128, True),    # the DiT's shape: 512 text tokens
+    (2, 1000, 77, 3, 128, False),    # partial query and key blocks
+    (1, 2048, 512, 2, 64, True),     # D = 64 (single-SM kernel)
+])
+def test_cross_attention_kernel_matches_fp32_attention(ops, shape):
+    """icsa_dit_cross_attention (the dense tcgen05 attention kernel without
+    order table, block table or residual) against softmax attention in fp32:
+    max-abs <= 2e-2 and mean-abs <= 1e-3, the tolerance of the attention
+    output in bf16."""
+    B, Lq, Lk, H, D, strided = shape
+    g = torch.Generator(device="cuda").manual_seed(Lq + Lk + D)
+    q = torch.randn(B, Lq, H, D, device="cuda", generator=g).to(torch.bfloat16)
+    if strided:
+        kv = torch.randn(B * Lk, 2 * H * D, device="cuda", generator=g).to(torch.bfloat16)
+        k = kv[:, :H * D].view(B, Lk, H, D)
+        v = kv[:, H * D:].view(B, Lk, H, D)
+        assert v.stride(1) == 2 * H * D
+    else:
+        k, v = (torch.randn(B, Lk, H, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(2))
+    got = ops.cross_attention(q, k, v)
+    torch.cuda.synchronize()
+    ref = ReferenceOps.cross_attention(q, k, v)
+    s = torch.einsum("blhd,bkhd->bhlk", q.float(), k.float()) / D ** 0.5
+    exact = torch.einsum("bhlk,bkhd->blhd", s.softmax(-1), v.float())
+    d = (got.float() - exact).abs()
+    print(f"cross attention {shape}: max|d|={float(d.max()):.3e} mean|d|={float(d.mean()):.3e}")
+    assert got.shape == (B, Lq, H, D) and got.dtype == torch.bfloat16
+    assert float(d.max()) <= 2e-2 and float(d.mean()) <= 1e-3
+    assert float((got.float() - ref.float()).abs().mean()) <= 1e-3
