@@ -296,7 +296,7 @@ def dit_seq_len(latent):
     the 480p latent: 32760 | 32760 | 16), so that 8 ranks hold whole blocks."""
     t = latent[1] * (latent[2] // 2) * (latent[3] // 2)
     return -(-2 * t // 512) * 512
-DIT_LAUNCHES_PER_BLOCK = 9 + 1 + 13  # 3 LayerNorm, 3 RMSNorm/RoPE, 3 residual passes, the cross-attention + one
+DIT_LAUNCHES_PER_BLOCK = 9 + 1 + 13  # 3 LayerNorm, 3 RMSNorm/RoPE, 3 projections with the residual update, the cross-attention + one
                                      # unaligned attention call
 
 
@@ -409,7 +409,7 @@ def run_dit_step(args, world, rank, local):
                            "qk_exchange": "f32" if args.dit_f32_exchange or args.dit_no_pipeline
                            else "bf16 + f32 block means",
                            "l2": "every step streams 28 GB of weights; no flush"},
-                "roofline": {"bound": "tensor", "kernel": "whole step (cuBLAS GEMMs + this library's kernels)",
+                "roofline": {"bound": "tensor", "kernel": "whole step (cuBLAS GEMMs for q|k|v, cross q, cross k|v and FFN-in; this library for the rest)",
                              "achieved": achieved, "peak": sustained, "unit": "TFLOP/s per GPU",
                              "frac": achieved / sustained, "peak_kind": f"{src} sustained bf16",
                              "flops_per_step": flops, "attention_flops_per_step": attn_flops, "traffic": None},

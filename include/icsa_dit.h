@@ -135,6 +135,28 @@ ICSA_API int icsa_dit_gated_residual(float* x, const void* y, int64_t ldy, int r
                                      const float* gate, int64_t gate_batch_stride, cudaStream_t stream);
 
 /*
+ * A linear layer with the residual update fused into its epilogue:
+ *     x[r, c] = x[r, c] + bf16( a[r, :] . w[c, :] + bias[c] ) * gate[b, c],
+ *     b = r / rows_per_batch  (gate NULL: x[r, c] + bf16(...)),
+ * the product and the sum rounded once each in float32.  Replaces the
+ * reference's output projections with their residual updates: the
+ * self-attention's `x + self.o(y) * e[2]` (model.py:175-176, :258-259), the
+ * cross-attention's `x + cross_attn(...)` (:262 with the o-projection :188)
+ * and the FFN's `x + ffn(...) * e[5]` (:263-265); the nn.Linear runs in
+ * bf16 under autocast (float32 accumulation and bias, one rounding to bf16).
+ * The bf16 layer output never reaches memory.  tcgen05 GEMM on SM pairs
+ * (256 x 256 output tiles, persistent), float32 accumulation in TMEM.
+ *   a:    bf16 [M, lda] (K columns used);  w: bf16 [N, ldw] (nn.Linear weight)
+ *   bias: bf16 [N] or NULL;  x: float32 [M, ldx], updated in place
+ *   gate: float32, row b at b * gate_batch_stride, or NULL
+ * N must be a multiple of 32, K and lda / ldw multiples of 8, ldx and
+ * gate_batch_stride multiples of 4; buffers 16-byte aligned.
+ */
+ICSA_API int icsa_dit_linear_residual(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,
+                                      float* x, int64_t ldx, int M, int N, int K, int rows_per_batch,
+                                      const float* gate, int64_t gate_batch_stride, cudaStream_t stream);
+
+/*
  * Softmax attention of q over k, v with the default 1/sqrt(D) scale and no
  * mask: the DiT's cross-attention over the text tokens.  Replaces the
  * reference's flash_attention call (wanx/attention.py:18-85) made by

@@ -148,6 +148,22 @@ int encode_rows_map(CUtensorMap* m, const void* base, int B, int rows, int H, in
   return ICSA_OK;
 }
 
+// bf16 [rows, cols] row-major with leading dimension ld (elements), box
+// {64, 128}: 128 rows x 64 columns (one 128-byte swizzled row each).
+int encode_matrix_map(CUtensorMap* m, const void* base, int rows, int cols, int64_t ld) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return fail(ICSA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ICSA_ERR_CUDA, "cuTensorMapEncodeTiled (matrix map) failed with %d", int(r));
+  return ICSA_OK;
+}
+
 // bf16 [BH, n, D] with a {64, 128, 1} box (64 features x 128 pooled rows).
 int encode_pooled_map(CUtensorMap* m, const void* base, int BH, int n, int D) {
   EncodeTiledFn enc = get_encode_fn();
@@ -630,8 +646,39 @@ int icsa_dit_cross_attention(const void* q, int64_t q_row_stride, const void* k,
   return e == cudaSuccess ? ICSA_OK : cuda_fail(e, "cross attention");
 }
 
+int icsa_dit_linear_residual(const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias, float* x,
+                             int64_t ldx, int M, int N, int K, int rows_per_batch, const float* gate,
+                             int64_t gate_batch_stride, cudaStream_t stream) {
+  if (a == nullptr || w == nullptr || x == nullptr)
+    return fail(ICSA_ERR_INVALID, "linear_residual: a, w and x must be non-NULL");
+  if (M < 0 || N < 32 || N % 32 != 0 || K < 8 || K % 8 != 0 || rows_per_batch < 1)
+    return fail(ICSA_ERR_INVALID, "linear_residual: M=%d N=%d K=%d rows_per_batch=%d (N a multiple of 32, K of 8)", M,
+                N, K, rows_per_batch);
+  if (lda < K || lda % 8 != 0 || ldw < K || ldw % 8 != 0 || ldx < N || ldx % 4 != 0)
+    return fail(ICSA_ERR_INVALID, "linear_residual: leading dimensions (lda, ldw multiples of 8 and >= K; ldx a "
+                                  "multiple of 4 and >= N)");
+  if (gate != nullptr && (gate_batch_stride < 0 || gate_batch_stride % 4 != 0))
+    return fail(ICSA_ERR_INVALID, "linear_residual: gate_batch_stride must be a non-negative multiple of 4");
+  const void* ptrs[5] = {a, w, bias, x, gate};
+  for (int i = 0; i < 5; ++i)
+    if ((reinterpret_cast<uintptr_t>(ptrs[i]) & 15u) != 0)
+      return fail(ICSA_ERR_INVALID, "linear_residual: buffers must be 16-byte aligned");
+  if (M == 0) return ICSA_OK;
+  CUtensorMap am, wm;
+  int rc;
+  if ((rc = encode_matrix_map(&am, a, M, K, lda)) != ICSA_OK) return rc;
+  if ((rc = encode_matrix_map(&wm, w, N, K, ldw)) != ICSA_OK) return rc;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "linear_residual: device query");
+  e = icsa::launch_linear_residual(M, N, K, am, wm, static_cast<const __nv_bfloat16*>(bias), x, ldx, gate,
+                                   gate_batch_stride, rows_per_batch, sms, stream);
+  return e == cudaSuccess ? ICSA_OK : cuda_fail(e, "linear_residual");
+}
+
 int icsa_last_status(cudaStream_t stream, int clear) {
-  constexpr int kUnits = 4;
+  constexpr int kUnits = 5;
   static std::mutex mu;
   static int* addr[kMaxDevices][kUnits] = {};
   cudaError_t e = cudaStreamSynchronize(stream);
@@ -642,7 +689,8 @@ int icsa_last_status(cudaStream_t stream, int clear) {
   std::lock_guard<std::mutex> lock(mu);
   if (addr[dev][0] == nullptr) {
     cudaError_t (*const get[kUnits])(int**) = {icsa::sticky_status_dense_pair, icsa::sticky_status_flat,
-                                               icsa::sticky_status_sparse, icsa::sticky_status_selftest};
+                                               icsa::sticky_status_sparse, icsa::sticky_status_selftest,
+                                               icsa::sticky_status_gemm};
     int* a[kUnits] = {};
     for (int i = 0; i < kUnits; ++i)
       if ((e = get[i](&a[i])) != cudaSuccess) return cuda_fail(e, "sticky status address");

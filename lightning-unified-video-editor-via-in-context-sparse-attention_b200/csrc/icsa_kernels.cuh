@@ -114,11 +114,20 @@ cudaError_t launch_dense_pair_attention(const AttnParams& p, const AttnMaps& map
 // Block-sparse tiles (exact top_k blocks + interval term), P kept in TMEM.
 cudaError_t launch_sparse_attention(const AttnParams& p, const AttnMaps& maps, int D, cudaStream_t stream);
 
+// ------------------------------------------------- DiT output projections --
+// x[r, c] += bf16(a[r, :] . w[c, :] + bias[c]) * gate[r / rows_per_batch, c]
+// (gate nullptr: + bf16(...)); a_map / w_map: bf16 [M, K] / [N, K] with
+// {64, 128} boxes and 128-byte swizzle.
+cudaError_t launch_linear_residual(int M, int N, int K, const CUtensorMap& a_map, const CUtensorMap& w_map,
+                                   const __nv_bfloat16* bias, float* x, int64_t ldx, const float* gate,
+                                   int64_t gate_bs, int rows_per_batch, int num_sms, cudaStream_t stream);
+
 // Device addresses of the per-device sticky status words of the translation
 // units whose kernels have bounded waits (see report_error).
 cudaError_t sticky_status_dense_pair(int** out);
 cudaError_t sticky_status_flat(int** out);
 cudaError_t sticky_status_sparse(int** out);
 cudaError_t sticky_status_selftest(int** out);
+cudaError_t sticky_status_gemm(int** out);
 
 }  // namespace icsa

@@ -218,6 +218,15 @@ ICSA_DEV void tma_load_4d(void* dst, const CUtensorMap* map, uint32_t bar_cluste
       : "memory");
 }
 
+// 2-D form of tma_load_4d.
+ICSA_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
+      : "memory");
+}
+
 // Named barrier over `count` threads (whole warps).
 ICSA_DEV void named_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

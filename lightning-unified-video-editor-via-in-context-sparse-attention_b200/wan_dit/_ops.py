@@ -23,7 +23,7 @@ import torch.nn.functional as F
 from in_context_sparse_attention import _capi
 
 DIT_EXPORTED = ("icsa_dit_modulated_norm", "icsa_dit_norm_rope", "icsa_dit_norm_rope_pool",
-                "icsa_dit_gated_residual", "icsa_dit_cross_attention")
+                "icsa_dit_gated_residual", "icsa_dit_cross_attention", "icsa_dit_linear_residual")
 
 _DT = {torch.bfloat16: _capi.ICSA_BF16, torch.float32: _capi.ICSA_F32}
 
@@ -75,6 +75,8 @@ def _load():
     lib.icsa_dit_gated_residual.restype = i
     lib.icsa_dit_cross_attention.argtypes = [vp, i64, vp, i64, vp, i64, vp, i, i, i, i, i, vp]
     lib.icsa_dit_cross_attention.restype = i
+    lib.icsa_dit_linear_residual.argtypes = [vp, i64, vp, i64, vp, vp, i64, i, i, i, i, vp, i64, vp]
+    lib.icsa_dit_linear_residual.restype = i
     return lib
 
 
@@ -211,6 +213,29 @@ class CudaOps:
         gp, gbs = (gate.data_ptr(), gate.stride(0)) if gate is not None else (None, 0)
         _capi.check(self.lib.icsa_dit_gated_residual(x.data_ptr(), y.data_ptr(), ldy, rows, C, rows_per_batch, gp, gbs,
                                                      _stream()), "icsa_dit_gated_residual")
+        return x
+
+    def linear_residual_(self, x, a, w, b, gate, rows_per_batch):
+        """x (f32 [rows, N], in place) += bf16(a @ w^T + b) * gate[row // rows_per_batch]
+        (gate None: + bf16(...)): the output projection and its residual
+        update in one tcgen05 GEMM whose epilogue reads and writes x
+        (icsa_dit_linear_residual); a: bf16 [rows, K] row-major view,
+        w: bf16 [N, K] (nn.Linear weight), b: bf16 [N] or None."""
+        rows, lda = _rows(a)
+        N, K = w.shape
+        if x.dtype != torch.float32 or not x.is_contiguous() or x.shape != (rows, N):
+            raise ValueError(f"linear_residual_: x must be contiguous f32 [{rows}, {N}]")
+        if a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or a.shape[1] != K or w.stride(1) != 1:
+            raise ValueError("linear_residual_: a and w must be bf16 with matching K")
+        if b is not None and (b.dtype != torch.bfloat16 or b.shape != (N,) or not b.is_contiguous()):
+            raise ValueError(f"linear_residual_: bias must be bf16 [{N}]")
+        if gate is not None and (gate.dtype != torch.float32 or gate.shape[-1] != N or gate.stride(-1) != 1
+                                 or gate.shape[0] < -(-rows // rows_per_batch)):
+            raise ValueError("linear_residual_: gate must be f32 [batches, N]")
+        gp, gbs = (gate.data_ptr(), gate.stride(0)) if gate is not None else (None, 0)
+        _capi.check(self.lib.icsa_dit_linear_residual(
+            a.data_ptr(), lda, w.data_ptr(), w.stride(0), b.data_ptr() if b is not None else None, x.data_ptr(),
+            x.stride(0), rows, N, K, rows_per_batch, gp, gbs, _stream()), "icsa_dit_linear_residual")
         return x
 
     # --- attention ---------------------------------------------------------

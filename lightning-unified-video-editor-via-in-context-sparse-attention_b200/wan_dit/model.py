@@ -256,11 +256,14 @@ class WanDiT:
         n, hp = self.world, H // self.world
         e = self.e_block(blk, e0)
 
-        # self-attention (model.py:255-259)
+        # self-attention (model.py:255-259); the output projection and the
+        # residual update x + y * e[2] are one GEMM with a fused epilogue
         xin = ops.modulated_norm(x, e["scale0"], e["shift0"], s, cfg.eps, round_norm=first)
         dev = x.device
+        if x.dtype != torch.float32:
+            x = x.float()
         if n > 1 and self.pipelined:
-            y = self._self_attention_pipelined(blk, xin, B, s, t_seq_len)
+            self._self_attention_pipelined(blk, xin, B, s, t_seq_len, x, e["gate0"])
         else:
             qkv = ops.linear(xin, blk.w_qkv, blk.b_qkv)
             q, k, v, gate = self._qkv(blk, qkv, B, s)
@@ -269,11 +272,8 @@ class WanDiT:
             del q, k, v
             o = ops.self_attention(qf, kf, vf, alpha, t_seq_len)
             del qf, kf, vf
-            y = ops.linear(self._exchange_out(o), blk.w_o, blk.b_o)
+            ops.linear_residual_(x, self._exchange_out(o), blk.w_o, blk.b_o, e["gate0"], s)
             del o
-        if x.dtype != torch.float32:
-            x = x.float()
-        ops.gated_residual_(x, y, e["gate0"], s)
 
         # cross-attention (model.py:262, WanT2VCrossAttention :181-188)
         xn = ops.modulated_norm(x, blk.norm3_w, blk.norm3_b, s, cfg.eps)
@@ -285,15 +285,13 @@ class WanDiT:
         ops.norm_rope([(qc, blk.cnorm_q, False, qn)], rows_per_batch=s, eps=cfg.eps)
         ops.norm_rope([(kv[:, :C], blk.cnorm_k, False, kn)], rows_per_batch=L, eps=cfg.eps)
         oc = ops.cross_attention(qn.view(B, s, H, D), kn.view(B, L, H, D), kv[:, C:].view(B, L, H, D))
-        y = ops.linear(oc.reshape(B * s, C), blk.wc_o, blk.bc_o)
-        ops.gated_residual_(x, y, None, s)
+        ops.linear_residual_(x, oc.reshape(B * s, C), blk.wc_o, blk.bc_o, None, s)
 
         # FFN (model.py:263-265)
         xn = ops.modulated_norm(x, e["scale1"], e["shift1"], s, cfg.eps)
         h = ops.gelu_tanh(ops.linear(xn, blk.w1, blk.b1))
-        y = ops.linear(h, blk.w2, blk.b2)
+        ops.linear_residual_(x, h, blk.w2, blk.b2, e["gate1"], s)
         del h
-        ops.gated_residual_(x, y, e["gate1"], s)
         return x
 
     def _qkv(self, blk: _Block, qkv, B, s):
@@ -335,7 +333,7 @@ class WanDiT:
                                 token_pos=self.token_pos, splits=self.rope_splits, gate=(qkv[:, 3 * C], gate))
         return q, k, v, gate, qm, km
 
-    def _self_attention_pipelined(self, blk: _Block, xin, B, s, t_seq_len):
+    def _self_attention_pipelined(self, blk: _Block, xin, B, s, t_seq_len, x, res_gate):
         """Ulysses self-attention with the exchanges of one batch element
         overlapping the computation of the other: NCCL runs the all-to-alls on
         its own stream, each launched as soon as its operand is written, and
@@ -345,7 +343,9 @@ class WanDiT:
             projection+RoPE b0 | projection+RoPE b1 | attention b0 | attention b1 | o-proj b0 | o-proj b1
                                | exchange-in b0     | exchange-in b1 | exchange-out b0 | exchange-out b1
 
-        Every rank issues the same collectives in the same order."""
+        The o-projection of batch element b updates its rows of the residual
+        stream x in place (x + o(y) * res_gate[b]).  Every rank issues the same
+        collectives in the same order."""
         ops, g = self.ops, self.group
         cfg = self.cfg
         C, D, n = cfg.dim, cfg.head_dim, self.world
@@ -394,12 +394,11 @@ class WanDiT:
             inbound[b] = None
             r = torch.empty(n, s, hp, D, dtype=torch.bfloat16, device=xin.device)
             outbound.append((dist.all_to_all_single(r, o[0], group=g, async_op=True), r))
-        y = torch.empty(B * s, C, dtype=torch.bfloat16, device=xin.device)
         for b in range(B):
             work, r = outbound[b]
             work.wait()
-            y[b * s:(b + 1) * s] = ops.linear(r.permute(1, 0, 2, 3).reshape(s, C), blk.w_o, blk.b_o)
-        return y
+            ops.linear_residual_(x[b * s:(b + 1) * s], r.permute(1, 0, 2, 3).reshape(s, C), blk.w_o, blk.b_o,
+                                 res_gate[b:b + 1], s)
 
     @staticmethod
     def e_block(blk: _Block, e0):

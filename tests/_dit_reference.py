@@ -136,6 +136,9 @@ class ReferenceOps:
             x.copy_(x + y * self._per_row(gate, x.shape[0], rows_per_batch))
         return x
 
+    def linear_residual_(self, x, a, w, b, gate, rows_per_batch):
+        return self.gated_residual_(x, self.linear(a, w, b), gate, rows_per_batch)
+
     def self_attention(self, q, k, v, alpha, t_seq_len, means=None):
         if self._attention is not None:
             if means is not None:

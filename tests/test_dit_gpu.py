@@ -268,3 +268,39 @@ def test_cross_attention_kernel_matches_fp32_attention(ops, shape):
     assert got.shape == (B, Lq, H, D) and got.dtype == torch.bfloat16
     assert float(d.max()) <= 2e-2 and float(d.mean()) <= 1e-3
     assert float((got.float() - ref.float()).abs().mean()) <= 1e-3
+
+
+@pytest.mark.parametrize("shape", [
+    # M, N, K, batches, gate, bias
+    (512, 256, 128, 1, True, True),
+    (1000, 768, 520, 2, True, True),     # partial row tile, K not a multiple of 64, two batches
+    (777, 512, 256, 1, False, False),    # no gate (cross-attention o-projection), no bias
+    (4096, 5120, 5120, 2, True, True),   # the DiT's o-projection shape on 32 rank-local tokens x 128
+])
+def test_linear_residual_matches_library_gemm_then_residual(ops, shape):
+    """icsa_dit_linear_residual (tcgen05 GEMM with the residual update in its
+    epilogue) against cuBLAS (F.linear, bf16 out) followed by the float32
+    update.  The bf16 layer output can differ by one bf16 unit where the two
+    float32 accumulations straddle a rounding boundary, so each element of x
+    may differ by at most one unit of y times |gate| (plus the float32
+    rounding of the sum), and such elements must be a small fraction."""
+    M, N, K, nb, use_gate, use_bias = shape
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    a = (torch.randn(M, K, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) * K ** -0.5).to(torch.bfloat16)
+    b = (torch.randn(N, device="cuda", generator=g) * 0.1).to(torch.bfloat16) if use_bias else None
+    x0 = torch.randn(M, N, device="cuda", generator=g)
+    gate = torch.randn(nb, N, device="cuda", generator=g) if use_gate else None
+    rpb = -(-M // nb)
+    got = ops.linear_residual_(x0.clone(), a, w, b, gate, rpb)
+    y = torch.nn.functional.linear(a, w, b)
+    ref = ReferenceOps().gated_residual_(x0.clone(), y, gate, rpb)
+    torch.cuda.synchronize()
+    gv = gate[torch.arange(M, device="cuda") // rpb] if use_gate else torch.ones(M, N, device="cuda")
+    ulp = torch.ldexp(torch.ones_like(y.float()), torch.frexp(y.float().abs().clamp_min(1e-30))[1] - 8)
+    bound = ulp * gv.abs() * 1.01 + ref.abs() * 2.0 ** -22 + 1e-30
+    d = (got - ref).abs()
+    frac = float((d > 0).float().mean())
+    print(f"linear_residual {shape}: max|d|={float(d.max()):.3e} differing={frac:.4f}")
+    assert bool((d <= bound).all()), float((d / bound).max())
+    assert frac <= 0.05
