@@ -535,28 +535,48 @@ class NumaLocal:
 
 
 def measure_link(host_in, host_out, dev, barrier, reps=3):
-    """Pinned host <-> device copy rates of this rank (GB/s), with every rank
-    copying at the same time (barrier before each direction): plain
-    contiguous copies of the same byte counts as one e2e step."""
+    """Pinned host <-> device copies of this rank's step bytes, with every
+    rank copying at the same time (barrier before each measurement): the
+    H2D rate and the D2H rate alone (GB/s), and the time (ms) of both
+    directions at once on two streams, which is what an e2e step needs at
+    the least (its copies in and out overlap)."""
     dins = [torch.empty_like(h, device=dev) for h in host_in]
     dout = torch.empty_like(host_out, device=dev)
+    h2d = list(zip(dins, host_in))
+    d2h = [(host_out, dout)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    rates = []
-    for direction in ("h2d", "d2h"):
-        pairs = list(zip(dins, host_in)) if direction == "h2d" else [(host_out, dout)]
-        nbytes = sum(h.numel() * h.element_size() for _, h in pairs)
-        for dst, src in pairs:  # one untimed pass
-            dst.copy_(src, non_blocking=True)
-        barrier()
-        e0.record()
+
+    def run(pairs):
         for _ in range(reps):
             for dst, src in pairs:
                 dst.copy_(src, non_blocking=True)
+
+    rates = []
+    for pairs in (h2d, d2h):
+        nbytes = sum(src.numel() * src.element_size() for _, src in pairs)
+        run(pairs[:1])  # untimed
+        barrier()
+        e0.record()
+        run(pairs)
         e1.record()
         barrier()
         rates.append(reps * nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+    # both directions at once
+    side = torch.cuda.Stream(device=dev)
+    barrier()
+    e0.record()
+    side.wait_event(e0)
+    with torch.cuda.stream(side):
+        run(d2h)
+    run(h2d)
+    done = torch.cuda.Event()
+    done.record(side)
+    torch.cuda.current_stream().wait_event(done)
+    e1.record()
+    barrier()
+    both_ms = e0.elapsed_time(e1) / reps
     del dins, dout
-    return rates[0], rates[1]
+    return rates[0], rates[1], both_ms
 
 
 def time_reference_dense(q, k, v, num_flat, tkv, steps):
@@ -729,9 +749,7 @@ def main():
                "d2h_bytes_per_step": q.numel() * q.element_size() * world}
         # the host link's rates with every rank copying at once, and the floor
         # they put under e2e: the slower direction of this rank's bytes
-        h2d_gbs, d2h_gbs = measure_link((hq, hk, hv), hout, dev, barrier)
-        rank_in, rank_out = 3 * q.numel() * q.element_size(), q.numel() * q.element_size()
-        floor = max(rank_in / (h2d_gbs * 1e9), rank_out / (d2h_gbs * 1e9)) * 1e3
+        h2d_gbs, d2h_gbs, floor = measure_link((hq, hk, hv), hout, dev, barrier)
         link = [h2d_gbs, d2h_gbs, floor]
         if dist is not None:
             gathered = [torch.zeros(3, device=dev) for _ in range(world)]
@@ -741,7 +759,9 @@ def main():
             link = [link]
         e2e["link"] = {"h2d_gbs_per_rank": [r[0] for r in link], "d2h_gbs_per_rank": [r[1] for r in link],
                        "floor_ms": max(r[2] for r in link),
-                       "measured": "pinned contiguous copies of each rank's step bytes, all ranks at once",
+                       "measured": "pinned contiguous copies of each rank's step bytes, all ranks at once; rates "
+                                   "per direction alone, floor_ms = both directions at once on two streams "
+                                   "(max over ranks)",
                        "numa_bound_cpus": numa.node}
 
     ms = elapsed / args.steps

@@ -12,11 +12,13 @@
 // bf16 y and the separate residual pass over the float32 stream disappear.
 //
 // Tiles: a cluster of two CTAs computes a 256 x 256 tile of the output, each
-// CTA 128 rows; per K step of 64 each CTA loads its 128 x 64 slice of a and
-// its 128 x 64 half of the 256 weight rows with TMA (16 KB each, 128-byte
-// swizzle), and the leader issues four M = 256, N = 256, K = 16 MMAs for the
-// pair.  Per SM that is 32 KB of shared memory read by the tensor core and
-// 32 KB written by TMA per 512 clk of tensor work.
+// CTA 128 rows; per K step of 128 each CTA loads its 128 x 128 slice of a and
+// its 128 x 128 half of the 256 weight rows with TMA (two 64-wide atoms of
+// 16 KB each, 128-byte swizzle), and the leader issues eight M = 256,
+// N = 256, K = 16 MMAs for the pair.  Per SM that is 64 KB of shared memory
+// read by the tensor core and 64 KB written by TMA per 1024 clk of tensor
+// work; one wait and one commit per 1024 clk keep the MMA warp's own
+// overheads off the tensor core's path.
 //
 // The kernel is persistent: every cluster walks the tile list with a stride
 // of the cluster count, in groups of kGGroupM tile rows (tile rows fastest
@@ -44,14 +46,23 @@ namespace {
 constexpr int kGThreads = 192;
 constexpr int kGProducerWarp = 4;
 constexpr int kGMmaWarp = 5;
-constexpr int kGStages = 6;
+#ifndef ICSA_GEMM_ATOMS
+#define ICSA_GEMM_ATOMS 2
+#endif
+#ifndef ICSA_GEMM_GROUP_M
+#define ICSA_GEMM_GROUP_M 8
+#endif
+constexpr int kGAtoms = ICSA_GEMM_ATOMS;             // 64-wide K atoms (128-byte swizzled rows) per stage
+constexpr int kGStages = 6 / kGAtoms;
 constexpr int kGRows = 128;                          // output rows per CTA (256 per pair)
 constexpr int kGCols = 256;                          // output columns per pair tile
-constexpr int kGKStep = 64;                          // K per stage: one 128-byte swizzled row
-constexpr int kGABytes = kGRows * kGKStep * 2;       // 16 KB
-constexpr int kGBBytes = (kGCols / 2) * kGKStep * 2; // 16 KB: this CTA's half of the weight rows
+constexpr int kGAtomK = 64;                          // K of one atom
+constexpr int kGKStep = kGAtomK * kGAtoms;           // K per stage
+constexpr int kGAtomBytes = 128 * kGAtomK * 2;       // 16 KB: 128 rows of one atom
+constexpr int kGABytes = kGAtoms * kGAtomBytes;      // this CTA's 128 rows of a
+constexpr int kGBBytes = kGAtoms * kGAtomBytes;      // this CTA's 128 of the 256 weight rows
 constexpr uint32_t kGTmemCols = 512;                 // two accumulators of 256 columns
-constexpr int kGGroupM = 8;                          // tile rows per raster group
+constexpr int kGGroupM = ICSA_GEMM_GROUP_M;          // tile rows per raster group
 
 enum : int { kErrGFull = 0x301, kErrGEmpty = 0x302, kErrGAccFull = 0x303, kErrGAccEmpty = 0x304, kErrGDrain = 0x305 };
 
@@ -109,16 +120,20 @@ ICSA_DEV void gemm_producer(const GemmParams& p, const GemmMaps& maps, GSmem& sm
       }
       if (rank == 0) mbar_arrive_expect_tx(&sm.full[s], 2 * (kGABytes + kGBBytes));
       const uint32_t full = pair::mapa(&sm.full[s], 0);
-      pair::tma_load_2d(sm.a[s], &maps.a, full, kb * kGKStep, row0);
-      pair::tma_load_2d(sm.b[s], &maps.w, full, kb * kGKStep, wrow0);
+#pragma unroll
+      for (int at = 0; at < kGAtoms; ++at) {
+        pair::tma_load_2d(sm.a[s] + at * kGAtomBytes, &maps.a, full, kb * kGKStep + at * kGAtomK, row0);
+        pair::tma_load_2d(sm.b[s] + at * kGAtomBytes, &maps.w, full, kb * kGKStep + at * kGAtomK, wrow0);
+      }
     }
   }
   *issued = it;
 }
 
-// Descriptor offsets of the four K = 16 steps inside a 128-byte swizzled row.
+// Descriptor offsets of the K = 16 steps: four inside each 128-byte swizzled
+// row, the next atom 16 KB further.
 template <int KK>
-constexpr uint32_t kGOff = uint32_t((KK * 32) >> 4);
+constexpr uint32_t kGOff = uint32_t(((KK >> 2) * kGAtomBytes + (KK & 3) * 32) >> 4);
 
 template <int... KK>
 ICSA_DEV void gemm_issue(uint64_t a_desc, uint64_t b_desc, uint32_t d_tmem, uint32_t acc,
@@ -148,7 +163,7 @@ ICSA_DEV void gemm_mma(const GemmParams& p, GSmem& sm, uint32_t tmem) {
       if (!pair::warp_wait(&sm.full[s], uint32_t(it / kGStages) & 1u, nullptr, kErrGFull, abort_flag)) return;
       tc::fence_after_sync();
       gemm_issue(ad0 + uint64_t(s) * kAStep, bd0 + uint64_t(s) * kBStep, d_tmem, kb > 0 ? 1u : 0u,
-                 std::make_integer_sequence<int, 4>{});
+                 std::make_integer_sequence<int, 4 * kGAtoms>{});
       pair::commit_both_elect(&sm.empty[s]);
     }
     pair::commit_both_elect(&sm.acc_full[buf]);
