@@ -92,7 +92,9 @@ typedef struct icsa_problem {
   int64_t alpha_strides[4]; /* tensor mode: element strides over [B,S,H,D], 0 = broadcast */
   int ca_bf16;              /* 1: out_compress*alpha is computed in bf16                  */
   /* options */
-  int debug_keys;           /* 1: keep the per-block selection scores in the workspace    */
+  int debug_keys;           /* no effect on the layout: the per-block selection scores
+                               are always in the workspace (blockscore); kept so that
+                               callers that set it keep working                         */
 } icsa_problem;
 
 /* Byte offsets of the named regions inside the workspace (for tests and
@@ -113,7 +115,7 @@ typedef struct icsa_workspace_layout {
   size_t kc, vc;     /* bf16 [B*H, nkv_pad, D] extended-KV block sums                */
   size_t sparse_idx; /* i32 [B*H, n_sparse, top_k] exact blocks per sparse q block  */
   size_t sel_mask;   /* u32 [B*H, n_sparse, nkv_pad/32] same, as a bit set           */
-  size_t blockscore; /* f32 [B*H, n_sparse, nkv] (debug_keys only, else 0)           */
+  size_t blockscore; /* f32 [B*H, n_sparse, nkv] per-sparse-block scores QC . KC^T   */
   size_t qbf, kbf, vbf;          /* bf16 [B,S,H,D] copies of f32 inputs (else 0)    */
   size_t newk, newv; /* bf16 [B, nkv*64, H, D] extended KV when t_seq_len % 64 != 0 */
   int nkv_pad;       /* nkv rounded up to a multiple of 128                          */

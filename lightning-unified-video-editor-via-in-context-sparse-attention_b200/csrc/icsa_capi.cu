@@ -97,7 +97,7 @@ void compute_layout(const icsa_problem* p, icsa_workspace_layout* w) {
   w->vc = take(BH * size_t(nkv_pad) * D * 2);
   w->sparse_idx = take(BH * size_t(n_sparse) * p->top_k * 4);
   w->sel_mask = take(BH * size_t(n_sparse) * (nkv_pad / 32) * 4);
-  w->blockscore = p->debug_keys ? take(BH * size_t(n_sparse) * p->nkv * 4) : 0;
+  w->blockscore = take(BH * size_t(n_sparse) * p->nkv * 4);
   const size_t act = size_t(p->B) * p->S * p->H * D * 2;
   w->qbf = p->q_dtype == ICSA_F32 ? take(act) : 0;
   w->kbf = p->k_dtype == ICSA_F32 ? take(act) : 0;
@@ -339,6 +339,10 @@ icsa::SelectParams make_select_params(const icsa_problem* p, const icsa_workspac
   s.k_src = p->k_dtype == ICSA_F32 ? at<__nv_bfloat16>(ws, L.kbf) : static_cast<const __nv_bfloat16*>(k);
   s.v_src = p->v_dtype == ICSA_F32 ? at<__nv_bfloat16>(ws, L.vbf) : static_cast<const __nv_bfloat16*>(v);
   s.newk = at<__nv_bfloat16>(ws, L.newk); s.newv = at<__nv_bfloat16>(ws, L.newv);
+  // the pool stage rounds the means to bf16 for bf16 inputs and for f32
+  // inputs whose compressed attention runs in bf16
+  s.means_bf16 = (p->q_dtype == ICSA_BF16 || p->outc_bf16) && (p->k_dtype == ICSA_BF16 || p->outc_bf16);
+  s.err = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + L.err);
   return s;
 }
 
@@ -678,7 +682,7 @@ int icsa_dit_linear_residual(const void* a, int64_t lda, const void* w, int64_t 
 }
 
 int icsa_last_status(cudaStream_t stream, int clear) {
-  constexpr int kUnits = 5;
+  constexpr int kUnits = 6;
   static std::mutex mu;
   static int* addr[kMaxDevices][kUnits] = {};
   cudaError_t e = cudaStreamSynchronize(stream);
@@ -690,7 +694,7 @@ int icsa_last_status(cudaStream_t stream, int clear) {
   if (addr[dev][0] == nullptr) {
     cudaError_t (*const get[kUnits])(int**) = {icsa::sticky_status_dense_pair, icsa::sticky_status_flat,
                                                icsa::sticky_status_sparse, icsa::sticky_status_selftest,
-                                               icsa::sticky_status_gemm};
+                                               icsa::sticky_status_gemm, icsa::sticky_status_scores};
     int* a[kUnits] = {};
     for (int i = 0; i < kUnits; ++i)
       if ((e = get[i](&a[i])) != cudaSuccess) return cuda_fail(e, "sticky status address");

@@ -55,18 +55,24 @@ struct SelectParams {
   __nv_bfloat16* vc;  // [BH, nkv_pad, D]
   int* sparse_idx;    // [BH, n_sparse, top_k]
   uint32_t* sel_mask; // [BH, n_sparse, nkv_pad / 32]
-  float* blockscore;  // [BH, n_sparse, nkv] or nullptr
+  float* blockscore;  // [BH, n_sparse, nkv] per-sparse-block scores
   // unaligned t_seq_len: materialised extended KV
   const __nv_bfloat16* k_src;  // bf16 [B, S, H, D] source of the gather
   const __nv_bfloat16* v_src;
   __nv_bfloat16* newk;         // [B, nkv*64, H, D]
   __nv_bfloat16* newv;
+  int means_bf16;              // qmean and kmean hold bf16 values (tensor-core scores)
+  int* err;                    // workspace status word (bounded waits)
 };
 
 // Compressed attention: scores, row statistics and in-context column sums on
 // `stream`; out_compress (which only the attention epilogue reads) on
 // `outc_stream`, which the caller orders after the row statistics.
 cudaError_t launch_compressed_scores(const SelectParams& p, cudaStream_t stream);
+// The scores alone on tcgen05 (means_bf16 and D = 64 or 128).
+cudaError_t launch_scores_tc(const SelectParams& p, cudaStream_t stream);
+// blockscore = QC[sparse blocks] . KC^T on tcgen05 (part of launch_sparse_topk).
+cudaError_t launch_blockscore_tc(const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_outc(const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_colsum(const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_selection(const SelectParams& p, cudaStream_t stream);
@@ -129,5 +135,6 @@ cudaError_t sticky_status_flat(int** out);
 cudaError_t sticky_status_sparse(int** out);
 cudaError_t sticky_status_selftest(int** out);
 cudaError_t sticky_status_gemm(int** out);
+cudaError_t sticky_status_scores(int** out);
 
 }  // namespace icsa

@@ -11,7 +11,8 @@
 //    from the stage-1 sums.  For t_seq_len % 64 != 0 the extended K/V are
 //    materialised (blocks straddle the target/source seam) and pooled again;
 //  * per-sparse-block top-k (tilelang_host.py:170-173): fp32
-//    QC . KC^T against every extended-KV block, keep top_k.
+//    QC . KC^T against every extended-KV block (a tensor-core block GEMM),
+//    keep top_k.
 #include "icsa_kernels.cuh"
 #include "icsa_sort.cuh"
 
@@ -110,76 +111,30 @@ __global__ void gather_extended_kernel(SelectParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// Per sparse query block: fp32 scores QC . KC^T against every extended-KV
-// block (tilelang_host.py:172), then the top_k blocks (:173) by a warp radix
-// select; ties go to the lower block index, and the selected set is written
-// in increasing block order together with its bit set.
+// Per sparse query block: the top_k extended-KV blocks (tilelang_host.py:173)
+// of its fp32 scores QC . KC^T (:172, computed on the tensor cores into
+// p.blockscore beforehand), by a warp radix select; ties go to the lower block
+// index, and the selected set is written in increasing block order together
+// with its bit set.
 //
-// CTA: `rows` (<= 8) sparse query blocks of one (b,h), 256 threads.  Scoring:
-// thread <-> extended-KV block, 8 query rows register-blocked, the query sums
-// transposed in shared memory ([D][8]) so each k value feeds 8 FMAs.
-// Selection: warp w <-> query block w.
+// CTA: `rows` (<= 8) sparse query blocks of one (b,h), warp w <-> query
+// block w; the CTA first stages the rows' order-preserving keys in shared
+// memory.
 // ---------------------------------------------------------------------------
 constexpr int kTopkThreads = 256;
 constexpr int kTopkRowsMax = 8;
 
 __global__ void __launch_bounds__(kTopkThreads) sparse_topk_kernel(SelectParams p, int rows) {
   extern __shared__ __align__(16) unsigned char sh_raw[];
-  const int D = p.D, nkv = p.nkv;
-  float* qT = reinterpret_cast<float*>(sh_raw);                                  // [D][8]
-  uint32_t* keys = reinterpret_cast<uint32_t*>(qT + D * kTopkRowsMax);           // [rows][nkv]
-  uint32_t* hist = keys + size_t(rows) * nkv;                                    // [8][256]
+  const int nkv = p.nkv;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(sh_raw);  // [rows][nkv]
+  uint32_t* hist = keys + size_t(rows) * nkv;             // [8][256]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y;
   const int r0 = blockIdx.x * rows;
-  const int* order = p.order + size_t(bh) * p.NB + p.num_flat;
-  for (int e = tid; e < kTopkRowsMax * D; e += kTopkThreads) {
-    const int r = e / D, d = e % D;
-    float v = 0.f;
-    if (r < rows && r0 + r < p.n_sparse)
-      v = __bfloat162float(p.qsum[(size_t(bh) * p.NB + order[r0 + r]) * D + d]);
-    qT[d * kTopkRowsMax + r] = v;
-  }
-  __syncthreads();
-  const __nv_bfloat16* KC = p.kc + size_t(bh) * p.nkv_pad * D;
-  for (int col = tid; col < nkv; col += kTopkThreads) {
-    float acc[kTopkRowsMax];
-#pragma unroll
-    for (int r = 0; r < kTopkRowsMax; ++r) acc[r] = 0.f;
-    const __nv_bfloat16* kr = KC + size_t(col) * D;
-    for (int d0 = 0; d0 < D; d0 += 8) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(kr + d0));
-      const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&u);
-      float kf[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(hv[i]);
-        kf[2 * i] = f.x;
-        kf[2 * i + 1] = f.y;
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float4 a = reinterpret_cast<const float4*>(qT)[(d0 + e) * 2];
-        const float4 b = reinterpret_cast<const float4*>(qT)[(d0 + e) * 2 + 1];
-        acc[0] = fmaf(a.x, kf[e], acc[0]);
-        acc[1] = fmaf(a.y, kf[e], acc[1]);
-        acc[2] = fmaf(a.z, kf[e], acc[2]);
-        acc[3] = fmaf(a.w, kf[e], acc[3]);
-        acc[4] = fmaf(b.x, kf[e], acc[4]);
-        acc[5] = fmaf(b.y, kf[e], acc[5]);
-        acc[6] = fmaf(b.z, kf[e], acc[6]);
-        acc[7] = fmaf(b.w, kf[e], acc[7]);
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < kTopkRowsMax; ++r) {
-      if (r < rows) {
-        keys[size_t(r) * nkv + col] = float_order_key(acc[r]);
-        if (p.blockscore != nullptr && r0 + r < p.n_sparse)
-          p.blockscore[(size_t(bh) * p.n_sparse + r0 + r) * nkv + col] = acc[r];
-      }
-    }
-  }
+  const int valid = min(rows, p.n_sparse - r0);
+  const float* bs = p.blockscore + (size_t(bh) * p.n_sparse + r0) * nkv;
+  for (int e = tid; e < valid * nkv; e += kTopkThreads) keys[e] = float_order_key(bs[e]);
   __syncthreads();
   if (warp >= rows || r0 + warp >= p.n_sparse) return;
   const int r = r0 + warp;
@@ -232,15 +187,16 @@ cudaError_t launch_extended_kv(const SelectParams& p, cudaStream_t stream) {
 cudaError_t launch_sparse_topk(const SelectParams& p, cudaStream_t stream) {
   if (p.n_sparse == 0) return cudaSuccess;
   const int BH = p.B * p.H;
+  cudaError_t e = launch_blockscore_tc(p, stream);
+  if (e != cudaSuccess) return e;
   auto smem_for = [&](int rows) {
-    return size_t(kTopkRowsMax) * p.D * sizeof(float) + size_t(rows) * p.nkv * sizeof(uint32_t) +
-           size_t(kTopkRowsMax) * 256 * sizeof(uint32_t);
+    return size_t(rows) * p.nkv * sizeof(uint32_t) + size_t(kTopkRowsMax) * 256 * sizeof(uint32_t);
   };
   int rows = kTopkRowsMax;
   while (rows > 1 && smem_for(rows) > 200 * 1024) --rows;
   const size_t smem = smem_for(rows);
   if (smem > 220 * 1024) return cudaErrorInvalidConfiguration;
-  cudaError_t e = cudaFuncSetAttribute(sparse_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  e = cudaFuncSetAttribute(sparse_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   dim3 g((p.n_sparse + rows - 1) / rows, BH);
   sparse_topk_kernel<<<g, kTopkThreads, smem, stream>>>(p, rows);

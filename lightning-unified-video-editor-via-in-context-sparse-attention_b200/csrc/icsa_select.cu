@@ -276,9 +276,15 @@ __global__ void colsum_kernel(SelectParams p) {
 
 cudaError_t launch_compressed_scores(const SelectParams& p, cudaStream_t stream) {
   const int BH = p.B * p.H;
-  dim3 g1((p.NB + kGT - 1) / kGT, (p.NB + kGT - 1) / kGT, BH);
-  scores_kernel<<<g1, 256, 0, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e;
+  if (p.means_bf16 && (p.D == 64 || p.D == 128)) {
+    e = launch_scores_tc(p, stream);
+  } else {
+    // f32 means: fp32 FMAs on the CUDA cores
+    dim3 g1((p.NB + kGT - 1) / kGT, (p.NB + kGT - 1) / kGT, BH);
+    scores_kernel<<<g1, 256, 0, stream>>>(p);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) return e;
 
   const int stride = p.n_t > 0 ? p.n_t : 1;
