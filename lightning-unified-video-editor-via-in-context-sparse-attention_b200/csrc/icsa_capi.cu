@@ -342,6 +342,7 @@ icsa::SelectParams make_select_params(const icsa_problem* p, const icsa_workspac
   // the pool stage rounds the means to bf16 for bf16 inputs and for f32
   // inputs whose compressed attention runs in bf16
   s.means_bf16 = (p->q_dtype == ICSA_BF16 || p->outc_bf16) && (p->k_dtype == ICSA_BF16 || p->outc_bf16);
+  s.vmean_bf16 = p->v_dtype == ICSA_BF16 || p->outc_bf16;
   s.err = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + L.err);
   return s;
 }

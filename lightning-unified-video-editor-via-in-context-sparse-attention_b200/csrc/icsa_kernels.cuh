@@ -62,6 +62,7 @@ struct SelectParams {
   __nv_bfloat16* newk;         // [B, nkv*64, H, D]
   __nv_bfloat16* newv;
   int means_bf16;              // qmean and kmean hold bf16 values (tensor-core scores)
+  int vmean_bf16;              // vmean holds bf16 values (tensor-core out_c)
   int* err;                    // workspace status word (bounded waits)
 };
 
@@ -71,6 +72,8 @@ struct SelectParams {
 cudaError_t launch_compressed_scores(const SelectParams& p, cudaStream_t stream);
 // The scores alone on tcgen05 (means_bf16 and D = 64 or 128).
 cudaError_t launch_scores_tc(const SelectParams& p, cudaStream_t stream);
+// out_c on tcgen05 (vmean_bf16 and D = 64 or 128; part of launch_outc).
+cudaError_t launch_outc_tc(const SelectParams& p, cudaStream_t stream);
 // blockscore = QC[sparse blocks] . KC^T on tcgen05 (part of launch_sparse_topk).
 cudaError_t launch_blockscore_tc(const SelectParams& p, cudaStream_t stream);
 cudaError_t launch_outc(const SelectParams& p, cudaStream_t stream);

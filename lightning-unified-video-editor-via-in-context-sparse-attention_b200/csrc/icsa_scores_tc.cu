@@ -247,6 +247,218 @@ cudaError_t launch_gemm(const GemmArgs& g, int D, int BH, cudaStream_t stream) {
   return cudaErrorInvalidValue;
 }
 
+
+// ---------------------------------------------------------------------------
+// out_c on the tensor cores (editing_sparse_attention.py:60-63):
+//
+//   out_c[bh, i, :] = sum_j P[i, j] Vc[bh, j, :],  P = exp(s - m_i) / l_i
+//
+// with P computed exactly as the CUDA-core kernel computes it (fp32,
+// 2^((s - m) log2 e) times 1/l).  P is split into two bf16 terms,
+// hi = bf16(P) and lo = bf16(P - hi), and both are multiplied by the bf16
+// values of Vc (the pooled means of bf16 values), so the products are exact
+// and the result carries P to about 16 bits (relative error below 2^-16 per
+// term) with fp32 accumulation.
+//
+// One CTA: 128 rows of one (b, h), 256 threads, keys in chunks of 64 through
+// two shared-memory stages {P_hi, P_lo, Vc}:
+//   * threads 0-127 (one row each) turn their row's 64 scores into P_hi/P_lo
+//     rows of the 128-byte-swizzled K-major A operands, with the next chunk's
+//     scores already loaded into registers;
+//   * threads 128-255 convert the chunk's 64 rows of Vc into the swizzled
+//     MN-major B operand (64 keys x D features);
+//   * after a barrier one elected lane issues 2 x 4 MMAs (M = 128, N = D,
+//     K = 16 keys) into the accumulator and commits them to the stage's
+//     mbarrier, which releases the stage two chunks later.
+// ---------------------------------------------------------------------------
+constexpr int kOKeys = 64;  // keys per chunk
+constexpr int kErrOutcMma = 0x203;
+
+template <int D>
+struct OutcSmem {
+  uint8_t phi[2][128 * 128];       // [stage][row][64 keys bf16], swizzled
+  uint8_t plo[2][128 * 128];
+  uint8_t v[2][D / 64][kOKeys * 128];  // [stage][d chunk][key][64 d bf16], swizzled
+  uint64_t mma_done[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int D, int... KK>
+ICSA_DEV void issue_outc(uint64_t hi_desc, uint64_t lo_desc, uint64_t v_desc, uint32_t d_tmem, uint32_t acc,
+                         std::integer_sequence<int, KK...>) {
+  constexpr uint32_t idesc = tc::make_idesc_bf16(128, D, false, true);
+  // A: 16 keys = 32 bytes along the swizzled row; B: 16 keys = 16 rows of 128 B
+  (tc::mma_bf16_ss_elect<uint32_t(KK * 2), uint32_t(KK * 128)>(d_tmem, hi_desc, v_desc, idesc,
+                                                               (KK > 0 || acc) ? 1u : 0u), ...);
+  (tc::mma_bf16_ss_elect<uint32_t(KK * 2), uint32_t(KK * 128)>(d_tmem, lo_desc, v_desc, idesc, 1u), ...);
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) outc_tc_kernel(SelectParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  OutcSmem<D>& sm = *reinterpret_cast<OutcSmem<D>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.y;
+  const int i0 = blockIdx.x * 128;
+  const int NB = p.NB;
+  const int n_chunks = (NB + kOKeys - 1) / kOKeys;
+  constexpr float kLog2e = 1.4426950408889634f;
+
+  if (warp == 0) {
+    tc::tmem_alloc(&sm.tmem_base, D);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&sm.mma_done[0], 1);
+    mbar_init(&sm.mma_done[1], 1);
+    sm.abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  // P rows: thread tid < 128 owns row i0 + tid
+  const bool prow = tid < 128;
+  const int i = i0 + (tid & 127);
+  const bool row_ok = prow && i < NB;
+  float m = 0.f, il = 0.f;
+  if (row_ok) {
+    m = p.rowmax[size_t(bh) * NB + i] * kLog2e;
+    il = 1.0f / p.rowsum[size_t(bh) * NB + i];
+  }
+  const float* srow = p.scores + (size_t(bh) * NB + (row_ok ? i : 0)) * NB;
+  const float* V = p.vmean + size_t(bh) * NB * D;
+  const bool vec = (NB & 3) == 0;  // every row starts on a 16-byte boundary
+  float4 raw[kOKeys / 4];          // this row's scores of the chunk being converted
+  auto load_scores = [&](int c) {
+    const int j0 = c * kOKeys;
+#pragma unroll
+    for (int e = 0; e < kOKeys / 4; ++e) {
+      const int j = j0 + 4 * e;
+      if (vec && row_ok && j + 3 < NB) {
+        raw[e] = __ldg(reinterpret_cast<const float4*>(srow + j));
+      } else {
+        // ragged end, or rows NB floats apart that do not keep 16-byte alignment
+        float t[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) t[q] = (row_ok && j + q < NB) ? srow[j + q] : 0.f;
+        raw[e] = make_float4(t[0], t[1], t[2], t[3]);
+      }
+    }
+  };
+  if (prow) load_scores(0);
+  __syncthreads();  // barriers initialised, TMEM allocated
+  tc::fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+
+  bool ok = true;
+#pragma unroll 1
+  for (int c = 0; c < n_chunks; ++c) {
+    const int st = c & 1;
+    const int j0 = c * kOKeys;
+    // the stage was last read by the MMAs of chunk c - 2
+    if (c >= 2 && ok) ok = mbar_wait(&sm.mma_done[st], uint32_t((c - 2) >> 1) & 1u, p.err, kErrOutcMma,
+                                     &sm.abort_flag);
+    if (prow) {
+      // raw holds chunk c; P = 2^(s log2e - m) / l, split into bf16 hi + lo
+      uint8_t* hrow = sm.phi[st] + tid * 128;
+      uint8_t* lrow = sm.plo[st] + tid * 128;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        float pv[8];
+        const float4 a = raw[2 * u], b = raw[2 * u + 1];
+        const float sv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int j = j0 + 8 * u + q;
+          float ex;
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(ex) : "f"(fmaf(sv[q], kLog2e, -m)));
+          pv[q] = (row_ok && j < NB) ? ex * il : 0.f;
+        }
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const __nv_bfloat16 h0 = __float2bfloat16_rn(pv[2 * q]), h1 = __float2bfloat16_rn(pv[2 * q + 1]);
+          hi[q] = uint32_t(__bfloat16_as_ushort(h0)) | (uint32_t(__bfloat16_as_ushort(h1)) << 16);
+          lo[q] = pack_bf16x2(pv[2 * q] - __bfloat162float(h0), pv[2 * q + 1] - __bfloat162float(h1));
+        }
+        const int off = (u ^ (tid & 7)) << 4;
+        *reinterpret_cast<uint4*>(hrow + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(lrow + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+      if (c + 1 < n_chunks) load_scores(c + 1);
+    } else {
+      // Vc rows j0 .. j0 + 63: unit (key k, 8 features from d8 * 8)
+      constexpr int kUnits = kOKeys * D / 8;
+      const int t = tid - 128;
+#pragma unroll 4
+      for (int u = t; u < kUnits; u += 128) {
+        const int k = u / (D / 8), d8 = u % (D / 8);
+        uint4 w = make_uint4(0u, 0u, 0u, 0u);
+        if (j0 + k < NB) {
+          const float4* src = reinterpret_cast<const float4*>(V + size_t(j0 + k) * D + d8 * 8);
+          const float4 x0 = __ldg(src), x1 = __ldg(src + 1);
+          w = make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w), pack_bf16x2(x1.x, x1.y),
+                         pack_bf16x2(x1.z, x1.w));
+        }
+        *reinterpret_cast<uint4*>(sm.v[st][d8 >> 3] + k * 128 + (((d8 & 7) ^ (k & 7)) << 4)) = w;
+      }
+    }
+    fence_proxy_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0 && __all_sync(0xffffffffu, ok) && !sm.abort_flag) {
+      tc::fence_after_sync();
+      const uint64_t hd = tc::make_sw128_desc(smem_u32(sm.phi[st]), 16, 1024);
+      const uint64_t ld = tc::make_sw128_desc(smem_u32(sm.plo[st]), 16, 1024);
+      const uint64_t vd = tc::make_sw128_desc(smem_u32(sm.v[st][0]), kOKeys * 128, 1024);
+      issue_outc<D>(hd, ld, vd, tmem, c > 0 ? 1u : 0u, std::make_integer_sequence<int, kOKeys / 16>{});
+      tc::mma_commit_elect(&sm.mma_done[st]);
+    }
+  }
+  // the last chunk's commit covers every MMA issued before it
+  const int last = n_chunks - 1;
+  if (ok) ok = mbar_wait(&sm.mma_done[last & 1], uint32_t(last >> 1) & 1u, p.err, kErrOutcMma, &sm.abort_flag);
+  __syncwarp();
+  if (warp < 4 && __all_sync(0xffffffffu, ok)) {
+    tc::fence_after_sync();
+    const int row = i0 + warp * 32 + lane;
+    float* O = p.outc + (size_t(bh) * NB + row) * D;
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t r[32];
+      tc::tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(32 * c), r);
+      tc::tmem_wait_ld();
+      if (row < NB) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 4)
+          *reinterpret_cast<float4*>(O + 32 * c + e) = make_float4(
+              __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+      }
+    }
+  } else if (!ok && tid == 0) {
+    // give MMAs still in flight a bounded time before their columns go
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(&sm.mma_done[last & 1], uint32_t(last >> 1) & 1u))
+      if (global_timer_ns() - t0 > 1000000000ull) {
+        report_error(p.err, kErrScoresDrain);
+        break;
+      }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, D);
+}
+
+template <int D>
+cudaError_t launch_outc_tc_d(const SelectParams& p, cudaStream_t stream) {
+  const size_t smem = sizeof(OutcSmem<D>) + 1024;
+  const cudaError_t e = cudaFuncSetAttribute(outc_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  const dim3 grid((p.NB + 127) / 128, p.B * p.H);
+  outc_tc_kernel<D><<<grid, 256, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_scores_tc(const SelectParams& p, cudaStream_t stream) {
@@ -274,6 +486,13 @@ cudaError_t launch_blockscore_tc(const SelectParams& p, cudaStream_t stream) {
   g.div = 0.f;
   g.err = p.err;
   return launch_gemm(g, p.D, p.B * p.H, stream);
+}
+
+cudaError_t launch_outc_tc(const SelectParams& p, cudaStream_t stream) {
+  if (p.NB <= 0 || p.B * p.H <= 0) return cudaSuccess;
+  if (p.D == 128) return launch_outc_tc_d<128>(p, stream);
+  if (p.D == 64) return launch_outc_tc_d<64>(p, stream);
+  return cudaErrorInvalidValue;
 }
 
 ICSA_DEFINE_STICKY_ACCESSOR(sticky_status_scores)

@@ -303,6 +303,8 @@ cudaError_t launch_compressed_scores(const SelectParams& p, cudaStream_t stream)
 }
 
 cudaError_t launch_outc(const SelectParams& p, cudaStream_t stream) {
+  if (p.vmean_bf16 && (p.D == 64 || p.D == 128)) return launch_outc_tc(p, stream);
+  // f32 means: fp32 FMAs on the CUDA cores
   dim3 g3((p.NB + kOR - 1) / kOR, p.B * p.H);
   if (p.D == 128) outc_kernel<128><<<g3, 256, 0, stream>>>(p);
   else if (p.D == 64) outc_kernel<64><<<g3, 256, 0, stream>>>(p);
