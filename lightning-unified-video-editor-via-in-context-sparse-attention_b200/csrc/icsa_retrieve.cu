@@ -31,7 +31,7 @@ __global__ void sort_select_kernel(const float* keys, int n, int keep, int* out,
   for (int i = threadIdx.x; i < pow2; i += blockDim.x)
     sh_keys[i] = (i < n) ? select_key(k[i], uint32_t(i)) : 0ull;
   __syncthreads();
-  bitonic_sort_desc(sh_keys, pow2, threadIdx.x, blockDim.x, BlockSync{});
+  bitonic_sort_desc(sh_keys, pow2, threadIdx.x, blockDim.x);
   for (int i = threadIdx.x; i < keep; i += blockDim.x) out[size_t(row) * keep + i] = int(select_key_index(sh_keys[i]));
 }
 

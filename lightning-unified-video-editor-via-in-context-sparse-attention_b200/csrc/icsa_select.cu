@@ -260,7 +260,21 @@ __global__ void colsum_kernel(SelectParams p) {
   float acc = 0.f;
   if (j < p.n_s) {
     const float* S = p.scores + size_t(bh) * p.NB * p.NB + p.n_t + j;
-    for (int i = g; i < p.n_t; i += 8) acc += expf(S[size_t(i) * p.NB] - M[i]) / L[i];
+    // this group's rows g, g + 8, ... in increasing order; eight rows' loads
+    // are issued before their terms are added
+    int i = g;
+    for (; i + 56 < p.n_t; i += 64) {
+      float s[8], mm[8], ll[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        s[u] = S[size_t(i + 8 * u) * p.NB];
+        mm[u] = M[i + 8 * u];
+        ll[u] = L[i + 8 * u];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc += expf(s[u] - mm[u]) / ll[u];
+    }
+    for (; i < p.n_t; i += 8) acc += expf(S[size_t(i) * p.NB] - M[i]) / L[i];
   }
   part[g][c] = acc;
   __syncthreads();

@@ -6,12 +6,16 @@
 namespace icsa {
 
 // ---------------------------------------------------------------------------
-// Bitonic sort, descending, over a shared-memory array of pow2 length, by a
-// group of `nthreads` threads (a warp or the whole CTA); `sync` is the
-// matching barrier.
+// Bitonic sort, descending, over a shared-memory array of pow2 length (>= 32)
+// by the `nthreads` threads of a CTA (a multiple of 32; thread t handles
+// elements t, t + nthreads, ...).  A compare-exchange stage of stride j < 32
+// pairs elements of one 32-aligned segment, and every element of a segment
+// is handled by one warp, so between two such stages a warp barrier
+// suffices; a CTA barrier follows every stage that has, or is followed by a
+// stage that has, a stride of 32 or more.
 // ---------------------------------------------------------------------------
-template <typename T, typename Sync>
-ICSA_DEV void bitonic_sort_desc(T* a, int n, int tid, int nthreads, Sync sync) {
+template <typename T>
+ICSA_DEV void bitonic_sort_desc(T* a, int n, int tid, int nthreads) {
   for (int k = 2; k <= n; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
       for (int i = tid; i < n; i += nthreads) {
@@ -25,17 +29,12 @@ ICSA_DEV void bitonic_sort_desc(T* a, int n, int tid, int nthreads, Sync sync) {
           }
         }
       }
-      sync();
+      const int next_j = j > 1 ? j >> 1 : k;  // first stride of the next k
+      if (j >= 32 || next_j >= 32 || k == n) __syncthreads();
+      else __syncwarp();
     }
   }
 }
-
-struct WarpSync {
-  ICSA_DEV void operator()() const { __syncwarp(); }
-};
-struct BlockSync {
-  ICSA_DEV void operator()() const { __syncthreads(); }
-};
 
 inline int next_pow2(int n) {
   int p = 32;
