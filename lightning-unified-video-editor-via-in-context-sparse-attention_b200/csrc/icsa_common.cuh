@@ -20,6 +20,31 @@ constexpr int kBlock = 64;          // BLOCK_M of the reference: tokens per bloc
 constexpr int kTileRows = 128;      // Q rows per attention tile (two 64-token blocks)
 
 // ---------------------------------------------------------------------------
+// Chained launches (programmatic dependent launch).  A kernel launched with
+// launch_chained may start while the kernel before it in the stream is still
+// finishing; it calls wait_prior_grid() before it reads anything that kernel
+// wrote (the wait returns once the prior grid has completed and its memory
+// is visible).  Kernels launched without the attribute pass the wait at once.
+// ---------------------------------------------------------------------------
+ICSA_DEV void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... Params, typename... Args>
+inline cudaError_t launch_chained(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
+// ---------------------------------------------------------------------------
 // Error reporting from device code.  Every bounded wait that gives up writes a
 // code into the call's status word `err` (first writer wins) and the kernel
 // winds down instead of hanging.

@@ -28,6 +28,7 @@ __global__ void sort_select_kernel(const float* keys, int n, int keep, int* out,
   extern __shared__ uint64_t sh_keys[];
   const int row = blockIdx.x;
   const float* k = keys + size_t(row) * n;
+  wait_prior_grid();
   for (int i = threadIdx.x; i < pow2; i += blockDim.x)
     sh_keys[i] = (i < n) ? select_key(k[i], uint32_t(i)) : 0ull;
   __syncthreads();
@@ -44,8 +45,7 @@ cudaError_t launch_sort_select(const float* keys, int rows, int n, int keep, int
     cudaError_t e = cudaFuncSetAttribute(sort_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
   }
-  sort_select_kernel<<<rows, 512, smem, stream>>>(keys, n, keep, out, pow2);
-  return cudaGetLastError();
+  return launch_chained(sort_select_kernel, dim3(rows), dim3(512), smem, stream, keys, n, keep, out, pow2);
 }
 
 // ---------------------------------------------------------------------------
@@ -58,6 +58,7 @@ __global__ void extended_kv_kernel(SelectParams p, int aligned) {
   const int bh = blockIdx.y;
   const int j = blockIdx.x;  // extended-KV block, 0 .. nkv_pad-1
   const size_t dst = (size_t(bh) * p.nkv_pad + j) * p.D;
+  wait_prior_grid();
   int src_block = -1;
   if (j < p.nkv) {
     if (aligned) {
@@ -86,6 +87,7 @@ __global__ void gather_extended_kernel(SelectParams p) {
   const int r = blockIdx.x;  // extended row
   const int b = blockIdx.y;
   const int HD = p.H * p.D;
+  wait_prior_grid();
   const int rows_ext = p.nkv * kBlock;
   for (int c = threadIdx.x * 8; c < HD; c += blockDim.x * 8) {
     const int h = c / p.D;
@@ -134,6 +136,7 @@ __global__ void __launch_bounds__(kTopkThreads) sparse_topk_kernel(SelectParams 
   const int r0 = blockIdx.x * rows;
   const int valid = min(rows, p.n_sparse - r0);
   const float* bs = p.blockscore + (size_t(bh) * p.n_sparse + r0) * nkv;
+  wait_prior_grid();
   for (int e = tid; e < valid * nkv; e += kTopkThreads) keys[e] = float_order_key(bs[e]);
   __syncthreads();
   if (warp >= rows || r0 + warp >= p.n_sparse) return;
@@ -175,13 +178,11 @@ cudaError_t launch_extended_kv(const SelectParams& p, cudaStream_t stream) {
   const int aligned = (p.t_seq_len % kBlock) == 0;
   if (!aligned) {
     dim3 g(p.nkv * kBlock, p.B);
-    gather_extended_kernel<<<g, 256, 0, stream>>>(p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_chained(gather_extended_kernel, g, dim3(256), 0, stream, p);
     if (e != cudaSuccess) return e;
   }
   dim3 g(p.nkv_pad, BH);
-  extended_kv_kernel<<<g, 128, 0, stream>>>(p, aligned);
-  return cudaGetLastError();
+  return launch_chained(extended_kv_kernel, g, dim3(128), 0, stream, p, aligned);
 }
 
 cudaError_t launch_sparse_topk(const SelectParams& p, cudaStream_t stream) {
@@ -199,8 +200,7 @@ cudaError_t launch_sparse_topk(const SelectParams& p, cudaStream_t stream) {
   e = cudaFuncSetAttribute(sparse_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   dim3 g((p.n_sparse + rows - 1) / rows, BH);
-  sparse_topk_kernel<<<g, kTopkThreads, smem, stream>>>(p, rows);
-  return cudaGetLastError();
+  return launch_chained(sparse_topk_kernel, g, dim3(kTopkThreads), smem, stream, p, rows);
 }
 
 }  // namespace icsa

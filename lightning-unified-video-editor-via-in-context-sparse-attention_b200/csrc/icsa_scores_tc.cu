@@ -168,6 +168,7 @@ __global__ void __launch_bounds__(kThreads) block_gemm_kernel(const GemmArgs g) 
     sm.abort_flag = 0;
     fence_mbarrier_init();
   }
+  wait_prior_grid();  // the operands are the previous kernels' outputs
   stage_operand<D, kTM>(sm.a, g.a, bh, i0);
   stage_operand<D, kTN>(sm.b, g.b, bh, j0);
   // the generic-proxy stores must be visible to the tensor core's reads
@@ -237,8 +238,7 @@ cudaError_t launch_gemm(const GemmArgs& g, int BH, cudaStream_t stream) {
       cudaFuncSetAttribute(block_gemm_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   const dim3 grid((g.b.rows + kTN - 1) / kTN, (g.a.rows + kTM - 1) / kTM, BH);
-  block_gemm_kernel<D><<<grid, kThreads, smem, stream>>>(g);
-  return cudaGetLastError();
+  return launch_chained(block_gemm_kernel<D>, grid, dim3(kThreads), smem, stream, g);
 }
 
 cudaError_t launch_gemm(const GemmArgs& g, int D, int BH, cudaStream_t stream) {

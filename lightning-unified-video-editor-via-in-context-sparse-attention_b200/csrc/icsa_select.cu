@@ -108,6 +108,7 @@ __global__ void rowstats_kernel(SelectParams p, int warps, int stride) {
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int bh = blockIdx.y;
   const int i = blockIdx.x * warps + warp;
+  wait_prior_grid();
   if (i >= p.NB) return;
   const float* S = p.scores + (size_t(bh) * p.NB + i) * p.NB;
   float m = -INFINITY;
@@ -257,6 +258,7 @@ __global__ void colsum_kernel(SelectParams p) {
   const int j = blockIdx.x * 32 + c;
   const float* M = p.rowmax + size_t(bh) * p.NB;
   const float* L = p.rowsum + size_t(bh) * p.NB;
+  wait_prior_grid();
   float acc = 0.f;
   if (j < p.n_s) {
     const float* S = p.scores + size_t(bh) * p.NB * p.NB + p.n_t + j;
@@ -312,8 +314,7 @@ cudaError_t launch_compressed_scores(const SelectParams& p, cudaStream_t stream)
     if (e != cudaSuccess) return e;
   }
   dim3 g2((p.NB + warps - 1) / warps, BH);
-  rowstats_kernel<<<g2, warps * 32, smem, stream>>>(p, warps, stride);
-  return cudaGetLastError();
+  return launch_chained(rowstats_kernel, g2, dim3(warps * 32), smem, stream, p, warps, stride);
 }
 
 cudaError_t launch_outc(const SelectParams& p, cudaStream_t stream) {
@@ -329,8 +330,7 @@ cudaError_t launch_outc(const SelectParams& p, cudaStream_t stream) {
 cudaError_t launch_colsum(const SelectParams& p, cudaStream_t stream) {
   if (p.n_s <= 0) return cudaSuccess;
   dim3 g4((p.n_s + 31) / 32, p.B * p.H);
-  colsum_kernel<<<g4, dim3(32, 8), 0, stream>>>(p);
-  return cudaGetLastError();
+  return launch_chained(colsum_kernel, g4, dim3(32, 8), 0, stream, p);
 }
 
 }  // namespace icsa
