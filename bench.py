@@ -56,7 +56,9 @@ from in_context_sparse_attention import _capi, editing_sparse_attention, shardin
 
 METRIC = "sparse-attn ms/call at 65K joint tokens (40h×128d bf16) 1/2/4/8 GPU; DiT step s"
 WORKLOADS = {"480p": synthetic.WAN480P, "720p": synthetic.WAN720P, "config1": synthetic.CONFIG1}
-KERNELS_PER_CALL_ALIGNED = 11  # pool, scores, rowstats, outc, colsum, 2x sort, extended-KV, top-k, dense + sparse attention
+# pool, scores GEMM, rowstats, out_c, colsum, 2x sort, extended-KV, block-score GEMM, top-k select,
+# dense + sparse attention
+KERNELS_PER_CALL_ALIGNED = 12
 
 
 def peaks():
@@ -484,7 +486,7 @@ def run_sweep(args, local):
                     rows.append(row)
                     # pool, scores, rowstats, outc, colsum, 2 sorts, extended KV; top-k and the sparse kernel only with
                     # sparse blocks, the dense kernel only with flat blocks
-                    launches += (8 + (2 if r.L.n_sparse else 0) + (1 if p.num_flat else 0)) * args.steps
+                    launches += (8 + (3 if r.L.n_sparse else 0) + (1 if p.num_flat else 0)) * args.steps
                     del r
             del q, k, v
             torch.cuda.empty_cache()
