@@ -45,7 +45,8 @@ cudaError_t launch_sort_select(const float* keys, int rows, int n, int keep, int
     cudaError_t e = cudaFuncSetAttribute(sort_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
   }
-  return launch_chained(sort_select_kernel, dim3(rows), dim3(512), smem, stream, keys, n, keep, out, pow2);
+  const int threads = pow2 < 1024 ? pow2 : 1024;  // one key per thread up to 1024 keys
+  return launch_chained(sort_select_kernel, dim3(rows), dim3(threads), smem, stream, keys, n, keep, out, pow2);
 }
 
 // ---------------------------------------------------------------------------

@@ -14,18 +14,18 @@
 // the lower index), so the summation order changes no contract, only low
 // bits of the keys.
 //
-// One CTA: 128 A rows x 256 B rows, 256 threads.
+// One CTA: 128 A rows x 128 B rows, 256 threads.
 //   1. all threads load their share of both operands (f32 rows are converted
 //      to bf16; bf16 rows are copied) into shared memory in the
 //      128-byte-swizzled K-major layout; A rows may be gathered through an
 //      index table;
-//   2. one elected lane of warp 0 issues D/16 MMAs (M = 128, N = 256, K = 16)
-//      into 256 TMEM columns and commits them to an mbarrier;
+//   2. one elected lane of warp 0 issues D/16 MMAs (M = 128, N = 128, K = 16)
+//      into 128 TMEM columns and commits them to an mbarrier;
 //   3. warps w and w + 4 read TMEM lanes [32 (w % 4), +32) (their A rows),
 //      alternate 32-column chunks, divide by the divisor if one is given, and
 //      write the tile through a shared-memory transpose so that each store
 //      instruction covers 128 contiguous bytes of one output row.
-// Two CTAs fit on an SM (97 KB of shared memory and 256 TMEM columns each).
+// Three CTAs fit on an SM (65 KB of shared memory and 128 TMEM columns each).
 #include "icsa_kernels.cuh"
 #include "icsa_tcgen05.cuh"
 
@@ -37,16 +37,23 @@ namespace icsa {
 namespace {
 
 constexpr int kTM = 128;       // A rows per CTA (TMEM lanes)
-constexpr int kTN = 256;       // B rows per CTA (TMEM columns)
+// B rows per CTA (TMEM columns).  128 rather than 256: twice the CTAs and
+// half the epilogue per CTA measured 4-25 us faster for the scores GEMM
+// (5-40 heads of 480p), the extra reads of A coming from L2.
+constexpr int kTN = 128;
 constexpr int kThreads = 256;  // warps w and w + 4 share TMEM lanes [32 (w % 4), +32)
 constexpr int kErrScoresMma = 0x201;
 constexpr int kErrScoresDrain = 0x202;
+
+constexpr int kStageBytes = 8 * 32 * 33 * 4;  // the epilogue's transpose buffers
 
 template <int D>
 struct ScoresSmem {
   // D/64 chunks of 64 features; a row of a chunk is 128 bytes (64 bf16)
   uint8_t a[D / 64][kTM * 128];
   uint8_t b[D / 64][kTN * 128];
+  // the transpose buffers reuse a and b; this pads them where they are smaller
+  uint8_t pad[(D / 64) * (kTM + kTN) * 128 >= kStageBytes ? 16 : kStageBytes - (D / 64) * (kTM + kTN) * 128];
   uint64_t done;
   uint32_t tmem_base;
   int abort_flag;
@@ -187,8 +194,8 @@ __global__ void __launch_bounds__(kThreads) block_gemm_kernel(const GemmArgs g) 
   __syncwarp();
   if (__all_sync(0xffffffffu, ok)) {
     tc::fence_after_sync();
-    // transpose buffer of this warp, over the (now idle) operands (8 x 4.2 KB
-    // fit in the 48 KB of a and b for D = 64)
+    // transpose buffer of this warp, over the (now idle) operands and the
+    // padding after them
     float(*stg)[33] = reinterpret_cast<float(*)[33]>(sm.a[0] + warp * 32 * 33 * sizeof(float));
     float* out = g.out + bh * g.out_bh;
     const int quarter = warp & 3;  // TMEM lanes (A rows) this warp may read
