@@ -19,9 +19,10 @@
 //   S(j+1) once softmax(j) has read S(j), then P.V(j-1) once P(j-1) is written.
 //
 // Roles per CTA (384 threads):
-//   warps 0-3 / 4-7  softmax of key columns [0,64) / [64,128) of every row
-//                    (thread <-> TMEM lane <-> query row); the two halves of
-//                    a row exchange their maxima through shared memory;
+//   warps 0-3 / 4-7  softmax of the even / odd key steps, all 128 columns of
+//                    every row (thread <-> TMEM lane <-> query row); the
+//                    running maximum passes between the two warpgroups
+//                    through shared memory every step;
 //   warp 8           TMA producer (Q once, then the K and V rings);
 //   warp 9           TMEM allocation; in the leader, the MMA issuer.
 #include "icsa_attn_common.cuh"
