@@ -67,7 +67,7 @@ ICSA_DEV void store_f32x8(float* dst, const float (&f)[8]) {
 template <typename T>
 ICSA_DEV void pool_block(const PoolParams& p, const PoolTensor& t, int b, int nb) {
   const int HD = p.H * p.D;
-  const int col = (blockIdx.x * kPoolThreads + threadIdx.x) * 8;
+  const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (col >= HD) return;
   const int row0 = nb * kBlock;
   const int rows = min(kBlock, p.S - row0);
@@ -145,8 +145,11 @@ __global__ void __launch_bounds__(kPoolThreads) pool_kernel(PoolParams p) {
 cudaError_t launch_pool(const PoolParams& p, cudaStream_t stream) {
   const int HD = p.H * p.D;
   const int vec_lanes = HD / 8;
-  dim3 grid((vec_lanes + kPoolThreads - 1) / kPoolThreads, p.num_blocks, 3 * p.B);
-  pool_kernel<<<grid, kPoolThreads, 0, stream>>>(p);
+  // a row of few heads is narrower than 128 lanes: size the CTA to it (whole
+  // warps) so that more CTAs, and more loads, fit on an SM
+  const int threads = vec_lanes < kPoolThreads ? (vec_lanes + 31) / 32 * 32 : kPoolThreads;
+  dim3 grid((vec_lanes + threads - 1) / threads, p.num_blocks, 3 * p.B);
+  pool_kernel<<<grid, threads, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
