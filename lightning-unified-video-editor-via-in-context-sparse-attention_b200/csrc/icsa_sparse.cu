@@ -21,10 +21,15 @@
 //
 // Roles: warps 0-3 softmax + epilogue (thread t <-> row t <-> TMEM lane t);
 // warp 4 TMA producer; warp 5 TMEM allocator + MMA issuer.
-// TMEM: S double buffer [0,128) [128,256) (P of a step overwrites the first 64
-// columns of its S buffer), O [256,256+D) for the exact part, G [384,384+D) for
-// the interval part.  The MMA thread issues S(j+1) before P(j).V so the tensor
-// core computes the next scores while the softmax of step j runs.
+// TMEM: S double buffer [0,128) [128,256), O [256,256+D) for the exact part,
+// G [384,384+D) for the interval part.  P of exact step j goes to buffer j%2
+// at [384 + 64 (j%2), +64): G's columns are idle until the interval steps,
+// and there each row's other-block half of P stays zero from one store at
+// the start instead of being rewritten every step.  P of an interval step
+// overwrites the first 64 columns of its S buffer.  The MMA thread issues
+// S(j+1) before P(j).V so the tensor core computes the next scores while the
+// softmax of step j runs; S(j) complete implies P.V(j-2) complete, so P(j)
+// never overwrites a buffer still being read.
 #include "icsa_attn_common.cuh"
 
 #include <utility>
@@ -196,7 +201,8 @@ ICSA_DEV void sparse_mma(const AttnParams& p, const STile& t, SSmem<D>& sm, uint
     tc::fence_after_sync();
     const bool interval = j >= t.n_exact;
     const uint32_t acc = interval ? (j > t.n_exact) : (j > 0);
-    sparse_issue_pv_seq<D>(vd0 + uint64_t(st) * kStageStep, tmem + uint32_t(j & 1) * 128u,
+    sparse_issue_pv_seq<D>(vd0 + uint64_t(st) * kStageStep,
+                           interval ? tmem + uint32_t(j & 1) * 128u : tmem + kSColG + uint32_t(j & 1) * 64u,
                            tmem + (interval ? kSColG : kSColO), acc ? 1u : 0u, std::make_integer_sequence<int, 8>{});
     // v_empty also tells the softmax that P.V(j) is done (before an O rescale)
     tc::mma_commit_elect(&sm.v_empty[st]);
@@ -253,6 +259,15 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
   }
   const uint32_t* mask_row = mask_in_smem ? sm.mask[half]
                                           : p.sel_mask + (size_t(t.bh) * p.n_sparse + (half ? t.rank[1] : t.rank[0])) * words;
+  {
+    // exact-step P buffers b = 0, 1 live in G's columns [64 b, 64 b + 64)
+    // until the interval steps; the other block's half of each stays zero
+    uint32_t zero[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) zero[e] = 0u;
+    tc::tmem_st32(tmem + lanes + kSColG + (1 - half) * 32, zero);
+    tc::tmem_st32(tmem + lanes + kSColG + 64u + (1 - half) * 32, zero);
+  }
   bool staged = false;
   float m_ref = -INFINITY;   // exponent origin of O and l (raw score units)
   float m_true = -INFINITY;  // running max as the reference tracks it
@@ -315,14 +330,10 @@ ICSA_DEV void sparse_softmax(const AttnParams& p, const AttnMaps& maps, const ST
           tc::tmem_st32(tmem + lanes + kSColO + c * 32, r);
         }
       }
-      uint32_t pk[32], zero[32];
+      uint32_t pk[32];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        pk[e] = pack_bf16x2(s[2 * e], s[2 * e + 1]);
-        zero[e] = 0u;
-      }
-      tc::tmem_st32(s_col + half * 32, pk);
-      tc::tmem_st32(s_col + (1 - half) * 32, zero);
+      for (int e = 0; e < 32; ++e) pk[e] = pack_bf16x2(s[2 * e], s[2 * e + 1]);
+      tc::tmem_st32(tmem + lanes + kSColG + uint32_t(sb) * 64u + half * 32, pk);
     } else {
       if (!staged) {
         asm volatile("bar.sync 1, 128;" ::: "memory");
