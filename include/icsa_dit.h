@@ -110,10 +110,16 @@ ICSA_API int icsa_dit_norm_rope(const icsa_dit_norm_rope_desc* desc, cudaStream_
  *     b*mean_batch_stride + (h / heads_per_group)*mean_group_stride
  *       + ((h % heads_per_group)*(rows_per_batch/64) + k)*D + d
  * rows_per_batch must be a multiple of 64.  rs_scratch: float workspace of
- * count * rows entries (the per-row RMSNorm factors).  A sequence-parallel
- * caller exchanges bf16 vectors and float32 means instead of float32
- * vectors, and hands the means to the attention in place of the ones it
- * would pool from the bf16 values.
+ * count * rows entries (the per-row RMSNorm factors).
+ * Optionally, with sum[j] set, the bf16 sum of every block of the written
+ * bf16 values (rows summed in order in float32, rounded once: what icsa_pool
+ * writes as the block sums), at the same offsets; and with bf16_mean[j] set,
+ * mean[j] is instead the bf16-arithmetic mean bf16(bf16(sum) / 64) of the
+ * written bf16 values, what icsa_pool computes for a bf16 vector.
+ * A sequence-parallel caller exchanges bf16 vectors and these block
+ * statistics instead of float32 vectors, and hands them to the attention in
+ * place of its pooling stage (q and k: float32 means and bf16 sums; v: bf16
+ * means and sums).
  */
 typedef struct icsa_dit_norm_rope_pool_desc {
   icsa_dit_norm_rope_desc base;
@@ -121,6 +127,8 @@ typedef struct icsa_dit_norm_rope_pool_desc {
   int64_t mean_batch_stride, mean_group_stride;
   int round_mean_bf16;
   float* rs_scratch;
+  void* sum[3];          /* bf16 block sums, or NULL */
+  int bf16_mean[3];      /* 1: mean[j] in the bf16 arithmetic of a bf16 vector */
 } icsa_dit_norm_rope_pool_desc;
 
 ICSA_API int icsa_dit_norm_rope_pool(const icsa_dit_norm_rope_pool_desc* desc, cudaStream_t stream);

@@ -317,7 +317,9 @@ struct RopePoolArgs {
   NormRopeArgs n;            // sources, weights, rope, bf16 destinations and their strides
   const float* rs[3];        // per-row rsqrt factors of the normalised vectors
   float* mean[3];            // f32 block means, or nullptr
-  int64_t mb, mg;            // mean offset of (b, g): b*mb + g*mg + (hl*nbl + blk)*D + d
+  __nv_bfloat16* sum[3];     // bf16 block sums of the bf16 outputs, or nullptr
+  int bf16_mean[3];          // mean of the bf16 outputs in bf16 arithmetic
+  int64_t mb, mg;            // mean / sum offset of (b, g): b*mb + g*mg + (hl*nbl + blk)*D + d
   int nbl;                   // 64-token blocks per batch element
   int round_mean;
 };
@@ -346,10 +348,14 @@ __global__ void __launch_bounds__(kPoolThreadsDit) norm_rope_pool_kernel(RopePoo
   const int half = a.D >> 1;
   float wf[8];
   if (w != nullptr) load8(w + col, wf);
-  float sum[8];
+  float sum[8], sum_bf[8];  // of the float32 results / of their bf16 roundings
 #pragma unroll
-  for (int i = 0; i < 8; ++i) sum[i] = 0.f;
-  const bool pool = pa.mean[j] != nullptr;
+  for (int i = 0; i < 8; ++i) sum[i] = sum_bf[i] = 0.f;
+  // selects instead of dynamic indexing of the parameter arrays
+  float* mean_out = j == 0 ? pa.mean[0] : (j == 1 ? pa.mean[1] : pa.mean[2]);
+  __nv_bfloat16* sum_out = j == 0 ? pa.sum[0] : (j == 1 ? pa.sum[1] : pa.sum[2]);
+  const bool bf16_mean = (j == 0 ? pa.bf16_mean[0] : (j == 1 ? pa.bf16_mean[1] : pa.bf16_mean[2])) != 0;
+  const bool pool = mean_out != nullptr || sum_out != nullptr;
   __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.dst[j]) + b * a.sb + g * a.sg + int64_t(hl) * a.D + d;
 #pragma unroll 4
   for (int r = 0; r < 64; ++r) {
@@ -383,17 +389,28 @@ __global__ void __launch_bounds__(kPoolThreadsDit) norm_rope_pool_kernel(RopePoo
     store8_bf16(dst + int64_t(t_local) * a.st, n);
     if (pool) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sum[i] += n[i];
+      for (int i = 0; i < 8; ++i) {
+        sum[i] += n[i];
+        sum_bf[i] += bf16_round(n[i]);
+      }
     }
   }
   if (pool) {
-    float mean[8];
+    const int64_t o = b * pa.mb + g * pa.mg + (int64_t(hl) * pa.nbl + blk) * a.D + d;
+    if (mean_out != nullptr) {
+      float mean[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      mean[i] = sum[i] / 64.f;
-      if (pa.round_mean) mean[i] = bf16_round(mean[i]);
+      for (int i = 0; i < 8; ++i) {
+        if (bf16_mean) {
+          mean[i] = bf16_round(bf16_round(sum_bf[i]) / 64.f);
+        } else {
+          mean[i] = sum[i] / 64.f;
+          if (pa.round_mean) mean[i] = bf16_round(mean[i]);
+        }
+      }
+      store8_f32(mean_out + o, mean);
     }
-    store8_f32(pa.mean[j] + b * pa.mb + g * pa.mg + (int64_t(hl) * pa.nbl + blk) * a.D + d, mean);
+    if (sum_out != nullptr) store8_bf16(sum_out + o, sum_bf);
   }
 }
 
@@ -582,7 +599,11 @@ int icsa_dit_norm_rope_pool(const icsa_dit_norm_rope_pool_desc* pd, cudaStream_t
       return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: vector %d must be written as bf16", j);
     if (pd->mean[j] != nullptr && !aligned16(pd->mean[j]))
       return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: mean %d must be 16-byte aligned", j);
+    if (pd->sum[j] != nullptr && !aligned16(pd->sum[j]))
+      return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: sum %d must be 16-byte aligned", j);
     pa.mean[j] = reinterpret_cast<float*>(pd->mean[j]);
+    pa.sum[j] = reinterpret_cast<__nv_bfloat16*>(pd->sum[j]);
+    pa.bf16_mean[j] = pd->bf16_mean[j] ? 1 : 0;
     ra.src[j] = a.src[j];
     if (d->norm_weight[j] != nullptr) {
       if (pd->rs_scratch == nullptr) return dit_fail(ICSA_ERR_INVALID, "norm_rope_pool: rs_scratch is NULL");

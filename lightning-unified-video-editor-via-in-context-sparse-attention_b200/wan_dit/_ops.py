@@ -56,6 +56,8 @@ class NormRopePoolDesc(ctypes.Structure):
         ("mean_batch_stride", ctypes.c_int64), ("mean_group_stride", ctypes.c_int64),
         ("round_mean_bf16", ctypes.c_int),
         ("rs_scratch", ctypes.c_void_p),
+        ("sum", ctypes.c_void_p * 3),
+        ("bf16_mean", ctypes.c_int * 3),
     ]
 
 
@@ -133,24 +135,36 @@ class CudaOps:
         _capi.check(self.lib.icsa_dit_norm_rope(ctypes.byref(d), _stream()), "icsa_dit_norm_rope")
 
     def norm_rope_pool(self, jobs, means, rows_per_batch, eps, token_offset=0, table=None, token_pos=None,
-                       splits=(0, 0), gate=None, round_mean=True):
+                       splits=(0, 0), gate=None, round_mean=True, sums=None, bf16_mean=(False, False, False)):
         """norm_rope with bf16 outputs and, for each job whose entry of
         `means` is a tensor, the f32 means of its 64-token blocks, laid out
-        [B, G, hp, s/64, D] (include/icsa_dit.h, icsa_dit_norm_rope_pool)."""
+        [B, G, hp, s/64, D] (include/icsa_dit.h, icsa_dit_norm_rope_pool).
+        sums: optional bf16 tensors of the same shape for the block sums of
+        the bf16 outputs; bf16_mean[j]: mean j in the bf16 arithmetic of a
+        bf16 vector (the attention's pooling of v)."""
         base = self._norm_rope_desc(jobs, rows_per_batch, eps, token_offset, table, token_pos, splits, gate)
         B, G, s, hp, D = jobs[0][3].shape
         if s % 64:
             raise ValueError(f"norm_rope_pool: {s} tokens per batch element are not whole 64-token blocks")
         d = NormRopePoolDesc()
         d.base = base
+        shape = (B, G, hp, s // 64, D)
         ref = None
         for j, m in enumerate(means):
             if m is None:
                 continue
-            if m.shape != (B, G, hp, s // 64, D) or m.dtype != torch.float32 or not m.is_contiguous():
-                raise ValueError(f"norm_rope_pool: mean {j} must be contiguous f32 {(B, G, hp, s // 64, D)}")
+            if m.shape != shape or m.dtype != torch.float32 or not m.is_contiguous():
+                raise ValueError(f"norm_rope_pool: mean {j} must be contiguous f32 {shape}")
             d.mean[j] = m.data_ptr()
+            d.bf16_mean[j] = int(bool(bf16_mean[j]))
             ref = m
+        for j, m in enumerate(sums or ()):
+            if m is None:
+                continue
+            if m.shape != shape or m.dtype != torch.bfloat16 or not m.is_contiguous():
+                raise ValueError(f"norm_rope_pool: sum {j} must be contiguous bf16 {shape}")
+            d.sum[j] = m.data_ptr()
+            ref = m if ref is None else ref
         if ref is not None:
             d.mean_batch_stride, d.mean_group_stride = ref.stride(0), ref.stride(1)
         d.round_mean_bf16 = int(bool(round_mean))
@@ -251,7 +265,9 @@ class CudaOps:
         (icsa_dit_norm_rope_pool computes them before the exchange).  The
         pool stage then runs on the bf16 tensors, its q / k means are
         replaced by these, and the result is bit for bit the one of the f32
-        call."""
+        call.  With six arrays, (qmean, kmean, vmean, qsum, ksum, vsum)
+        (f32 means, bf16 sums, all [B, h, NB, D]), the pool stage does not
+        run at all: these are every block statistic it would produce."""
         if means is not None:
             return self._self_attention_premeaned(q, k, v, alpha, t_seq_len, means)
         B, S, H, D = q.shape
@@ -284,19 +300,26 @@ class CudaOps:
         p = self._problem(q, k, v, alpha, t_seq_len, _capi.ICSA_BF16, _capi.ICSA_BF16)
         L = _capi.workspace_layout(p)
         NB = p.num_blocks
-        qm, km = means
-        if qm.shape != (B, H, NB, D) or km.shape != (B, H, NB, D):
-            raise ValueError(f"self_attention means must be f32 [{B}, {H}, {NB}, {D}]")
+        if len(means) not in (2, 6) or any(m.shape != (B, H, NB, D) for m in means):
+            raise ValueError(f"self_attention means must be 2 or 6 arrays [{B}, {H}, {NB}, {D}]")
         lib, st = self.lib, _stream()
         size = L.total
         ws = torch.empty(size, dtype=torch.uint8, device=q.device)
         out = torch.empty(B, S, H, D, dtype=torch.bfloat16, device=q.device)
         pp = ctypes.byref(p)
         a = (q.data_ptr(), k.data_ptr(), v.data_ptr())
-        _capi.check(lib.icsa_pool(pp, *a, ws.data_ptr(), size, st), "icsa_pool")
-        n = B * H * NB * D * 4
-        ws[L.qmean:L.qmean + n].view(torch.float32).copy_(qm.reshape(-1))
-        ws[L.kmean:L.kmean + n].view(torch.float32).copy_(km.reshape(-1))
+        n = B * H * NB * D
+        regions = [(L.qmean, torch.float32), (L.kmean, torch.float32)]
+        if len(means) == 6:
+            # every block statistic of the pool stage is given: it does not run
+            regions += [(L.vmean, torch.float32), (L.qsum, torch.bfloat16), (L.ksum, torch.bfloat16),
+                        (L.vsum, torch.bfloat16)]
+        else:
+            _capi.check(lib.icsa_pool(pp, *a, ws.data_ptr(), size, st), "icsa_pool")
+        for (off, dt), m in zip(regions, means):
+            if m.dtype != dt:
+                raise ValueError(f"self_attention: block statistic of dtype {m.dtype}, expected {dt}")
+            ws[off:off + n * m.element_size()].view(dt).copy_(m.reshape(-1))
         _capi.check(lib.icsa_select(pp, a[1], a[2], ws.data_ptr(), size, st), "icsa_select")
         _capi.check(lib.icsa_attend(pp, *a, alpha.data_ptr(), out.data_ptr(), ws.data_ptr(), size, st),
                     "icsa_attend")

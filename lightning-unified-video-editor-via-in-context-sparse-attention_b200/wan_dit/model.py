@@ -264,6 +264,8 @@ class WanDiT:
             x = x.float()
         if n > 1 and self.pipelined:
             self._self_attention_pipelined(blk, xin, B, s, t_seq_len, x, e["gate0"])
+        elif n == 1 and self.pooled_exchange and s % 64 == 0:
+            self._self_attention_local_pooled(blk, xin, B, s, t_seq_len, x, e["gate0"])
         else:
             qkv = ops.linear(xin, blk.w_qkv, blk.b_qkv)
             q, k, v, gate = self._qkv(blk, qkv, B, s)
@@ -312,11 +314,13 @@ class WanDiT:
         return q, k, v, gate
 
     def _qkv_pooled(self, blk: _Block, qkv, s):
-        """`_qkv` for one batch element with bf16 q, k and the f32 means of
-        their 64-token blocks, [1, world, H/world, s/64, D]: the block pooling
-        that the attention's first stage would take of the f32 q and k
-        (editing_sparse_attention.py:37-55, :107-111), done before the
-        exchange."""
+        """`_qkv` for one batch element with bf16 q, k, v and every block
+        statistic of the attention's first stage (editing_sparse_attention.py:
+        37-55, :107-111, and the block sums of tilelang_kernels.py:33-120),
+        [1, world, H/world, s/64, D] each, computed before the exchange: the
+        f32 means of the f32 q and k, the bf16-arithmetic mean of v, and the
+        bf16 block sums of q, k and v.  The attention then skips its pooling
+        pass over q, k and v."""
         cfg = self.cfg
         C, D, n = cfg.dim, cfg.head_dim, self.world
         hp = cfg.num_heads // n
@@ -324,14 +328,34 @@ class WanDiT:
         q = torch.empty(1, n, s, hp, D, dtype=torch.bfloat16, device=dev)
         k = torch.empty_like(q)
         v = torch.empty_like(q)
-        qm = torch.empty(1, n, hp, s // 64, D, dtype=torch.float32, device=dev)
-        km = torch.empty_like(qm)
+        means = [torch.empty(1, n, hp, s // 64, D, dtype=torch.float32, device=dev) for _ in range(3)]
+        sums = [torch.empty(1, n, hp, s // 64, D, dtype=torch.bfloat16, device=dev) for _ in range(3)]
         gate = torch.empty(s, dtype=torch.bfloat16, device=dev)
         self.ops.norm_rope_pool([(qkv[:, :C], blk.norm_q, True, q), (qkv[:, C:2 * C], blk.norm_k, True, k),
-                                 (qkv[:, 2 * C:3 * C], None, False, v)], [qm, km, None], rows_per_batch=s,
+                                 (qkv[:, 2 * C:3 * C], None, False, v)], means, rows_per_batch=s,
                                 eps=cfg.eps, token_offset=self.rank * s, table=self.rope_table,
-                                token_pos=self.token_pos, splits=self.rope_splits, gate=(qkv[:, 3 * C], gate))
-        return q, k, v, gate, qm, km
+                                token_pos=self.token_pos, splits=self.rope_splits, gate=(qkv[:, 3 * C], gate),
+                                sums=sums, bf16_mean=(False, False, True))
+        return q, k, v, gate, means + sums
+
+    def _self_attention_local_pooled(self, blk: _Block, xin, B, s, t_seq_len, x, res_gate):
+        """Self-attention on one rank holding the whole sequence, per batch
+        element: the producer pass writes bf16 q, k, v and every block
+        statistic of the attention's pooling stage, so the attention reads
+        bf16 operands and skips its pooling pass (the same bits as the f32
+        q / k call, as in the sequence-parallel path)."""
+        ops, cfg = self.ops, self.cfg
+        C, H, D = cfg.dim, cfg.num_heads, cfg.head_dim
+        for b in range(B):
+            qkv = ops.linear(xin[b * s:(b + 1) * s], blk.w_qkv, blk.b_qkv)
+            q, k, v, gate, stats = self._qkv_pooled(blk, qkv, s)
+            del qkv
+            # [1, 1, H, s/64, D] -> [1, H, s/64, D]
+            means = tuple(m[:, 0] for m in stats)
+            o = ops.self_attention(q.view(1, s, H, D), k.view(1, s, H, D), v.view(1, s, H, D), gate.view(1, s),
+                                   t_seq_len, means=means)
+            del q, k, v
+            ops.linear_residual_(x[b * s:(b + 1) * s], o.view(s, C), blk.w_o, blk.b_o, res_gate[b:b + 1], s)
 
     def _self_attention_pipelined(self, blk: _Block, xin, B, s, t_seq_len, x, res_gate):
         """Ulysses self-attention with the exchanges of one batch element
@@ -360,7 +384,7 @@ class WanDiT:
         for b in range(B):
             qkv = ops.linear(xin[b * s:(b + 1) * s], blk.w_qkv, blk.b_qkv)
             if pooled:
-                q, k, v, gate, qm, km = self._qkv_pooled(blk, qkv, s)
+                q, k, v, gate, stats = self._qkv_pooled(blk, qkv, s)
             else:
                 q, k, v, gate = self._qkv(blk, qkv, 1, s)
             del qkv
@@ -374,11 +398,9 @@ class WanDiT:
                      dist.all_gather_into_tensor(alpha.view(-1), gate, group=g, async_op=True)]
             means = None
             if pooled:
-                qmr = torch.empty(n, hp, s // 64, D, dtype=torch.float32, device=dev)
-                kmr = torch.empty_like(qmr)
-                works += [dist.all_to_all_single(qmr, qm[0], group=g, async_op=True),
-                          dist.all_to_all_single(kmr, km[0], group=g, async_op=True)]
-                means = (qmr, kmr)
+                # qmean, kmean, vmean (f32), qsum, ksum, vsum (bf16): [source rank, head, block, D]
+                means = tuple(torch.empty(n, hp, s // 64, D, dtype=x.dtype, device=dev) for x in stats)
+                works += [dist.all_to_all_single(r, x[0], group=g, async_op=True) for r, x in zip(means, stats)]
             inbound.append((works, qf, kf, vf, alpha, means))
         outbound = []
         for b in range(B):

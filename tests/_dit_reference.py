@@ -107,10 +107,12 @@ class ReferenceOps:
             gout.copy_((gsrc.sigmoid() - 0.5) * 0.5)
 
     def norm_rope_pool(self, jobs, means, rows_per_batch, eps, token_offset=0, table=None, token_pos=None,
-                       splits=(0, 0), gate=None, round_mean=True):
+                       splits=(0, 0), gate=None, round_mean=True, sums=None, bf16_mean=(False, False, False)):
         """norm_rope computed in f32, written as bf16, and the 64-token block
         means of the f32 values (compress_seq, editing_sparse_attention.py:
-        37-55 of the reference), laid out [B, G, hp, s/64, D]."""
+        37-55 of the reference), laid out [B, G, hp, s/64, D]; optionally the
+        bf16 block sums of the bf16 outputs (rows summed in order in f32) and,
+        with bf16_mean[j], mean j as bf16(bf16(sum) / 64) of the bf16 outputs."""
         f32 = []
         for src, w, rope, out in jobs:
             tmp = torch.empty(out.shape, dtype=torch.float32, device=out.device)
@@ -120,13 +122,33 @@ class ReferenceOps:
         if gate is not None:
             gsrc, gout = gate
             gout.copy_((gsrc.sigmoid() - 0.5) * 0.5)
-        for x, m in zip(f32, means):
+        sums = list(sums) if sums is not None else [None] * len(jobs)
+
+        def block_sum_in_order(x):
+            # [B, G, s, hp, D] -> [B, G, s/64, hp, D], rows of a block added one by one
+            B, G, s, hp, D = x.shape
+            xb = x.reshape(B, G, s // 64, 64, hp, D)
+            acc = torch.zeros(B, G, s // 64, hp, D, dtype=torch.float32, device=x.device)
+            for r in range(64):
+                acc = acc + xb[:, :, :, r]
+            return acc
+
+        for j, x in enumerate(f32):
+            m, sm = means[j] if j < len(means) else None, sums[j]
+            if m is None and sm is None:
+                continue
+            xb16 = x.to(torch.bfloat16).float()
+            sum_bf = block_sum_in_order(xb16)
+            if sm is not None:
+                sm.copy_(sum_bf.to(torch.bfloat16).permute(0, 1, 3, 2, 4))
             if m is None:
                 continue
-            B, G, s, hp, D = x.shape
-            mm = x.reshape(B, G, s // 64, 64, hp, D).sum(dim=3) / 64.0
-            if round_mean:
-                mm = mm.to(torch.bfloat16).float()
+            if bf16_mean[j]:
+                mm = (sum_bf.to(torch.bfloat16).float() / 64.0).to(torch.bfloat16).float()
+            else:
+                mm = block_sum_in_order(x) / 64.0
+                if round_mean:
+                    mm = mm.to(torch.bfloat16).float()
             m.copy_(mm.permute(0, 1, 3, 2, 4))
 
     def gated_residual_(self, x, y, gate, rows_per_batch):
@@ -144,7 +166,9 @@ class ReferenceOps:
             if means is not None:
                 return self._attention(q, k, v, alpha, t_seq_len, means=means)
             return self._attention(q, k, v, alpha, t_seq_len)
-        m = None if means is None else tuple(x.cpu().permute(0, 2, 1, 3) for x in means)
+        # the q / k means; the other block statistics of a six-array `means`
+        # are what the oracle's pooling computes from the bf16 tensors anyway
+        m = None if means is None else tuple(x.cpu().permute(0, 2, 1, 3) for x in means[:2])
         r = icsa_oracle.editing_sparse_attention(q.cpu(), k.cpu(), v.cpu(), t_seq_len,
                                                  alpha_2=alpha.cpu()[:, :, None, None], means=m)
         return r.out.to(torch.bfloat16).to(q.device).contiguous()

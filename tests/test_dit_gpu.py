@@ -195,7 +195,10 @@ def test_pooled_qk_give_the_f32_call_bit_for_bit(ops, grid, S, t_aligned):
     """The sequence-parallel exchange sends q and k as bf16 with the f32
     means of their 64-token blocks: the means equal those the pool stage
     takes of the f32 tensors, and the attention's output equals the f32
-    call's bit for bit (aligned and unaligned t_seq_len)."""
+    call's bit for bit (aligned and unaligned t_seq_len).  With the v means
+    and the bf16 block sums of q, k, v from the same producer pass, every
+    pooled statistic equals the pool stage's, and the attention without its
+    pooling pass still gives the same bits."""
     from wan_dit import head_dim_splits, rope_table, token_positions
     from _helpers import region
     from in_context_sparse_attention import editing_sparse_attention
@@ -235,6 +238,19 @@ def test_pooled_qk_give_the_f32_call_bit_for_bit(ops, grid, S, t_aligned):
     out_b = ops.self_attention(qb.view(B, S, H, D), kb.view(B, S, H, D), v_b.view(B, S, H, D), alpha, t,
                                means=(qm.view(B, H, NB, D), km.view(B, H, NB, D)))
     assert torch.equal(out_a, out_b)
+    # every block statistic of the pool stage from the producer pass: the
+    # attention then skips its pooling pass and still gives the same bits
+    stats = [torch.empty(B, 1, H, S // 64, D, device="cuda") for _ in range(3)]
+    sums = [torch.empty(B, 1, H, S // 64, D, dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+    ops.norm_rope_pool(jobs(qb, kb, v_b), stats, rows_per_batch=S, eps=1e-6, table=table, token_pos=pos,
+                       splits=splits, gate=(qkv[:, 3 * C], gate_b), sums=sums, bf16_mean=(False, False, True))
+    assert torch.equal(stats[0], qm) and torch.equal(stats[1], km)
+    for name, x, dt in (("vmean", stats[2], torch.float32), ("qsum", sums[0], torch.bfloat16),
+                        ("ksum", sums[1], torch.bfloat16), ("vsum", sums[2], torch.bfloat16)):
+        assert torch.equal(x.view(B, H, NB, D), region(dbg, name, dt, (B, H, NB, D))), name
+    out_c = ops.self_attention(qb.view(B, S, H, D), kb.view(B, S, H, D), v_b.view(B, S, H, D), alpha, t,
+                               means=tuple(x.view(B, H, NB, D) for x in stats + sums))
+    assert torch.equal(out_a, out_c)
 
 
 @pytest.mark.parametrize("shape", [
