@@ -11,18 +11,20 @@
 //
 // TMEM (512 columns per CTA):
 //   S at [0,128)                                  fp32 scores, lane = query row
-//   P(j) in buffer j%4 at [128 + 64 (j%4), +64)   bf16 pairs (A operand of P.V)
-//   O at [384,512)                                fp32 accumulator
-// Because P has its own columns, S(j+1) may overwrite S as soon as the
-// softmax has copied S(j) to registers, and with four P buffers P(j) never
-// waits for a recent P.V.  The tensor core's queue per step:
-//   S(j+1) once softmax(j) has read S(j), then P.V(j-1) once P(j-1) is written.
+//   P(j) in buffer j%2 at [128 + 64 (j%2), +64)   bf16 pairs (A operand of P.V)
+//   O_w at [256 + 128 w, +128), w = 0, 1          fp32 accumulators
+// Softmax warpgroup w owns the steps j with j % 2 == w, with P buffer w and
+// its own accumulator O_w, exponent origin and row sum, so the two
+// warpgroups never wait for each other; the epilogue brings O_0 and O_1 to
+// a common origin.  Because P has its own columns, S(j+1) may overwrite S as
+// soon as the softmax has copied S(j) to registers.  The tensor core's queue
+// per step:  S(j+1) once softmax(j) has read S(j), then P.V(j-1) once P(j-1)
+// is written.
 //
 // Roles per CTA (384 threads):
 //   warps 0-3 / 4-7  softmax of the even / odd key steps, all 128 columns of
-//                    every row (thread <-> TMEM lane <-> query row); the
-//                    running maximum passes between the two warpgroups
-//                    through shared memory every step;
+//                    every row (thread <-> TMEM lane <-> query row), each
+//                    into its own accumulator;
 //   warp 8           TMA producer (Q once, then the K and V rings);
 //   warp 9           TMEM allocation; in the leader, the MMA issuer.
 #include "icsa_attn_common.cuh"
@@ -43,12 +45,11 @@ constexpr int kPStages = 5;  // K/V ring: stage j % 5 holds this CTA's halves of
 constexpr int kPQBytes = 128 * 128 * 2;  // this CTA's 128 query rows, two 64-wide d chunks of 16 KB
 constexpr int kPKBytes = 64 * 128 * 2;   // 64 key rows x 128 d, two d chunks of 8 KB
 constexpr int kPVBytes = 128 * 64 * 2;   // 128 value rows x this CTA's 64 d
-constexpr uint32_t kTmS = 0, kTmP = 128, kTmO = 384, kPTmemCols = 512;
+constexpr uint32_t kTmS = 0, kTmP = 128, kTmO = 256, kPTmemCols = 512;
 
 struct __align__(1024) PSmem {
   uint8_t q[kPQBytes];
   uint8_t kv[kPStages][kPKBytes + kPVBytes];  // [K half | V half]
-  float mref[2][128];  // [warpgroup][row] m_ref after that warpgroup's latest step
   float ocs[2][128];   // per query block: out_c * alpha (scalar alpha) or out_c
   float lsum[2][128];  // epilogue: partial row sums and their origins
   float lmax[2][128];
@@ -57,7 +58,7 @@ struct __align__(1024) PSmem {
   // [w]: barriers of softmax warpgroup w (steps j with j % 2 == w), so each
   // is consumed in phase order by one party
   uint64_t s_full[2], s_free[2], p_full[2];
-  uint64_t pv_done[4];  // P.V(j) done, per P buffer j % 4
+  uint64_t pv_done[2];  // P.V(j) done, per P buffer j % 2
   uint64_t o_final;     // the last P.V done
   uint64_t mma_fin;
   uint32_t tmem_base;
@@ -176,9 +177,9 @@ ICSA_DEV void pair_mma(const AttnParams& p, const PTile& t, PSmem& sm, uint32_t 
     const int s = j % kPStages;
     if (!warp_mbar_wait(&sm.p_full[j & 1], uint32_t(j >> 1) & 1u, p.err, kErrPFull, abort_flag)) return false;
     tc::fence_after_sync();
-    pair_issue_pv_seq(vd0 + uint64_t(s) * kVStep, tmem + kTmP + 64u * uint32_t(j & 3), tmem + kTmO, j > 0 ? 1u : 0u,
-                      std::make_integer_sequence<int, 8>{});
-    pair::commit_both_elect(&sm.pv_done[j & 3]);
+    pair_issue_pv_seq(vd0 + uint64_t(s) * kVStep, tmem + kTmP + 64u * uint32_t(j & 1),
+                      tmem + kTmO + 128u * uint32_t(j & 1), j >= 2 ? 1u : 0u, std::make_integer_sequence<int, 8>{});
+    pair::commit_both_elect(&sm.pv_done[j & 1]);
     pair::commit_both_elect(&sm.kv_empty[s]);  // S(j) and P.V(j) have read stage s
     return true;
   };
@@ -199,30 +200,24 @@ ICSA_DEV void pair_mma(const AttnParams& p, const PTile& t, PSmem& sm, uint32_t 
 }
 
 // Softmax: warpgroup w handles the key steps j with j % 2 == w, over all 128
-// keys of the step (thread <-> TMEM lane <-> query row).  The running maximum
-// (the exponent origin m_ref of O) passes from one warpgroup to the other
-// every step through shared memory: the producer of step j publishes m_ref(j)
-// with a non-blocking named-barrier arrive and the consumer of step j+1
-// waits on the same barrier, so the two warpgroups run half a step apart and
-// one's loads and stores overlap the other's exponentials.
-// Each warpgroup keeps its own partial row sum l_w relative to the m_ref of
-// its last step; the epilogue brings both to the final origin.
-// Neither warpgroup may leave the loop early (the named barriers pair them):
-// after a failed wait the abort flag is set, every later wait returns at
-// once, the loop runs on over stale data, and the error code marks the
-// result invalid.
+// keys of the step (thread <-> TMEM lane <-> query row), into its own
+// accumulator O_w with its own exponent origin m_w (raised lazily, when a
+// step's maximum exceeds it by more than 2^8) and row sum l_w; the epilogue
+// brings both to the larger origin.  The warpgroups therefore never wait
+// for each other inside the loop.  Neither may leave the loop early (the
+// epilogue's named barriers pair them): after a failed wait the abort flag
+// is set, every later wait returns at once, the loop runs on over stale
+// data, and the error code marks the result invalid.
 ICSA_DEV void pair_softmax(const AttnParams& p, const AttnMaps& maps, const PTile& t, PSmem& sm, uint32_t tmem) {
   volatile int* abort_flag = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int w = warp >> 2;                 // this warpgroup's step parity
   const int row = threadIdx.x & 127;       // query row = TMEM lane
-  // named barriers 1-4: m_ref from warpgroup 0 to 1; 5-8: from 1 to 0 (per 32 rows)
-  const uint32_t bar_to_other = 1u + 4u * uint32_t(w) + uint32_t(warp & 3);
-  const uint32_t bar_from_other = 1u + 4u * uint32_t(w ^ 1) + uint32_t(warp & 3);
   const uint32_t lanes = uint32_t((warp & 3) * 32) << 16;
   const uint32_t s_base = tmem + lanes + kTmS;
-  const uint32_t p_base = tmem + lanes + kTmP + 64u * uint32_t(w);  // + 128 for odd own steps
-  const uint32_t o_base = tmem + lanes + kTmO;
+  const uint32_t p_base = tmem + lanes + kTmP + 64u * uint32_t(w);
+  const uint32_t o_base = tmem + lanes + kTmO;          // O_0 at +0, O_1 at +128
+  const uint32_t o_own = o_base + 128u * uint32_t(w);
   // the residual term of the epilogue, one value per thread: block row >> 6,
   // feature (row & 63) + 64 w (read after the epilogue's barrier 14)
   {
@@ -235,7 +230,7 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const AttnMaps& maps, const PTil
   const uint32_t p_full = pair::mapa(&sm.p_full[w], 0);
   const float sl2 = p.scale_log2;
   const int n = t.n_steps;
-  float m_w = -INFINITY, l_w = 0.f;  // partial row sum and its exponent origin
+  float m_w = -INFINITY, l_w = 0.f;  // this warpgroup's exponent origin and row sum
 
   for (int j = w; j < n; j += 2) {
     const uint32_t par = uint32_t(j >> 1) & 1u;
@@ -256,26 +251,13 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const AttnMaps& maps, const PTil
         if (c >= hi) s[c] = -INFINITY;
     }
     const float mx = max128(s);
-    float m_prev = -INFINITY;
-    if (j > 0) {
-      pair::named_sync(bar_from_other, 64);
-      m_prev = sm.mref[w ^ 1][row];
-    }
-    const bool need = (mx - m_prev) * sl2 > kRescaleThreshold;
-    const float m_ref = need ? mx : m_prev;
-    if (j + 1 < n) {
-      sm.mref[w][row] = m_ref;
-      pair::named_arrive(bar_to_other, 64);
-    }
-    if (m_w != m_ref) {
-      l_w = (m_w == -INFINITY) ? 0.f : l_w * ex2((m_w - m_ref) * sl2);
+    const bool need = (mx - m_w) * sl2 > kRescaleThreshold;
+    const float m_ref = need ? mx : m_w;
+    const float alpha = (need && m_w != -INFINITY) ? ex2((m_w - m_ref) * sl2) : 1.f;
+    if (need) {
+      l_w = (m_w == -INFINITY) ? 0.f : l_w * alpha;
       m_w = m_ref;
     }
-    // P buffer j%4 was last read by P.V(j-4) (issued before S(j), so in
-    // practice already complete)
-    const int pb = j & 3;
-    if (j >= 4) warp_mbar_wait(&sm.pv_done[pb], uint32_t((j - 4) >> 2) & 1u, p.err, kErrPvDone, abort_flag);
-    tc::fence_after_sync();
     const float neg = -m_ref * sl2;
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
@@ -288,31 +270,31 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const AttnMaps& maps, const PTil
       s[c + 3] = ex2(s[c + 3]);
       fadd2(a0, a1, a0, a1, s[c], s[c + 1]);
       fadd2(a2, a3, a2, a3, s[c + 2], s[c + 3]);
-      if ((c & 63) == 60) {
-        // 64 probabilities done: pack them and write them to the P buffer
-        uint32_t pk[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) pk[e] = pack_bf16x2(s[(c & ~63) + 2 * e], s[(c & ~63) + 2 * e + 1]);
-        tc::tmem_st32(p_base + 128u * uint32_t(pb >> 1) + uint32_t(c >> 6) * 32u, pk);
-      }
     }
     l_w += (a0 + a1) + (a2 + a3);
-    if (j > 0 && __any_sync(0xffffffffu, need)) {
-      // O holds P.V up to step j-1 relative to m_prev: rescale it to m_ref.
-      // The phase before P.V(j-1) on its barrier is P.V(j-5), issued before
-      // S(j), which has completed, so the parity wait is exact.
-      warp_mbar_wait(&sm.pv_done[(j - 1) & 3], uint32_t((j - 1) >> 2) & 1u, p.err, kErrPvDone, abort_flag);
+    // P buffer w and O_w were last used by P.V(j-2); the phase before it on
+    // its barrier, P.V(j-4), was issued before S(j-1) and has completed
+    if (j >= 2) {
+      warp_mbar_wait(&sm.pv_done[w], uint32_t((j - 2) >> 1) & 1u, p.err, kErrPvDone, abort_flag);
       tc::fence_after_sync();
-      const float alpha = need ? ex2((m_prev - m_ref) * sl2) : 1.f;
+      if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tc::tmem_ld32(o_base + 32u * uint32_t(c), r);
-        tc::tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tc::tmem_ld32(o_own + 32u * uint32_t(c), r);
+          tc::tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-        tc::tmem_st32(o_base + 32u * uint32_t(c), r);
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+          tc::tmem_st32(o_own + 32u * uint32_t(c), r);
+        }
       }
+    }
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      uint32_t pk[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) pk[e] = pack_bf16x2(s[64 * h2 + 2 * e], s[64 * h2 + 2 * e + 1]);
+      tc::tmem_st32(p_base + uint32_t(h2) * 32u, pk);
     }
     tc::tmem_wait_st();
     tc::fence_before_sync();
@@ -321,21 +303,19 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const AttnMaps& maps, const PTil
     __syncwarp();
   }
 
-  // epilogue: both partial sums to the final origin; this warpgroup writes
-  // features [64w, 64w + 64) of its row
-  const int last = n - 1;
+  // epilogue: both accumulators and row sums to the larger origin; this
+  // warpgroup writes features [64w, 64w + 64) of its row
   warp_mbar_wait(&sm.o_final, 0, p.err, kErrPvDone, abort_flag);
   tc::fence_after_sync();
   sm.lsum[w][row] = l_w;
   sm.lmax[w][row] = m_w;
   pair::named_sync(9u + uint32_t(warp & 3), 64);
-  const float m_fin = sm.lmax[last & 1][row];  // m_ref of the last step
-  float lt = 0.f;
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float mi = sm.lmax[i][row], li = sm.lsum[i][row];
-    if (mi != -INFINITY) lt += (mi == m_fin) ? li : li * ex2((mi - m_fin) * sl2);
-  }
+  const float m0 = sm.lmax[0][row], m1 = sm.lmax[1][row];
+  const float m_fin = fmaxf(m0, m1);
+  const bool has1 = n >= 2;  // O_1 holds data only when warpgroup 1 had steps
+  const float f0 = (m0 == -INFINITY) ? 0.f : ex2((m0 - m_fin) * sl2);
+  const float f1 = (!has1 || m1 == -INFINITY) ? 0.f : ex2((m1 - m_fin) * sl2);
+  const float lt = sm.lsum[0][row] * f0 + (has1 ? sm.lsum[1][row] * f1 : 0.f);
   const float inv = lt == 0.f ? 0.f : 1.0f / lt;
   const int hb = row >> 6;
   const int blk = hb ? t.blk[1] : t.blk[0];  // (no dynamic indexing: keeps the tile in registers)
@@ -357,10 +337,13 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const AttnMaps& maps, const PTil
       uint32_t r[32];
       __syncwarp();
       tc::tmem_ld32(o_base + 64u * uint32_t(w) + 32u * uint32_t(c), r);
+      uint32_t r1[32];
+      if (has1) tc::tmem_ld32(o_base + 128u + 64u * uint32_t(w) + 32u * uint32_t(c), r1);
       tc::tmem_wait_ld();
       float o[32], x[32];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(r[e]) * inv;
+      for (int e = 0; e < 32; ++e)
+        o[e] = (__uint_as_float(r[e]) * f0 + (has1 ? __uint_as_float(r1[e]) * f1 : 0.f)) * inv;
       if (valid_row && scalar) residual32_ca(oc, 64 * w + 32 * c, o, x);
       else if (valid_row) residual32(p, t.b, token, t.h, oc, 64 * w + 32 * c, o, x);
       else
@@ -399,10 +382,13 @@ ICSA_DEV void pair_softmax(const AttnParams& p, const AttnMaps& maps, const PTil
     uint32_t r[32];
     __syncwarp();
     tc::tmem_ld32(o_base + 64u * uint32_t(w) + 32u * uint32_t(c), r);
+    uint32_t r1[32];
+    if (has1) tc::tmem_ld32(o_base + 128u + 64u * uint32_t(w) + 32u * uint32_t(c), r1);
     tc::tmem_wait_ld();
     float o[32];
 #pragma unroll
-    for (int e = 0; e < 32; ++e) o[e] = __uint_as_float(r[e]) * inv;
+    for (int e = 0; e < 32; ++e)
+      o[e] = (__uint_as_float(r[e]) * f0 + (has1 ? __uint_as_float(r1[e]) * f1 : 0.f)) * inv;
     if (!write) continue;
     if (scalar) {
       float x[32];
@@ -447,7 +433,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       mbar_init(&sm.s_free[i], 8);  // one arrival per warp of the step's warpgroup, both CTAs
       mbar_init(&sm.p_full[i], 8);
     }
-    for (int i = 0; i < 4; ++i) mbar_init(&sm.pv_done[i], 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&sm.pv_done[i], 1);
     mbar_init(&sm.o_final, 1);
     mbar_init(&sm.mma_fin, 1);
     sm.abort_flag = 0;
