@@ -132,3 +132,33 @@ def test_ulysses_step_on_two_ranks_equals_one_rank():
             # the runs differ only in GEMM row blocking (bf16 outputs) and the
             # exchanges, which move bytes unchanged
             assert err <= 2e-2 * scale, (rank, err, scale)
+
+
+def test_reference_block_statistics_follow_the_pool_stage_arithmetic():
+    """The torch mirror of icsa_dit_norm_rope_pool (used by the CPU
+    sequence-parallel test) writes the block statistics with the pool stage's
+    arithmetic: bf16 block sums of the bf16 outputs (rows added in order in
+    float32, rounded once), the float32 means of q and k, and for v the mean
+    bf16(bf16(sum) / 64)."""
+    from _dit_reference import ReferenceOps
+    g = torch.Generator().manual_seed(4)
+    s, H, D = 128, 2, 64
+    C = H * D
+    src = torch.randn(s, C, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(C, generator=g)).to(torch.bfloat16)
+    q = torch.empty(1, 1, s, H, D, dtype=torch.bfloat16)
+    v = torch.empty_like(q)
+    qm, vm = (torch.empty(1, 1, H, s // 64, D) for _ in range(2))
+    qs, vs = (torch.empty(1, 1, H, s // 64, D, dtype=torch.bfloat16) for _ in range(2))
+    ReferenceOps().norm_rope_pool([(src, w, False, q), (src, None, False, v)], [qm, vm], rows_per_batch=s,
+                                  eps=1e-6, sums=[qs, vs], bf16_mean=(False, True))
+    for out, mean, sums, bf16_mean in ((q, qm, qs, False), (v, vm, vs, True)):
+        x = out[0, 0].float()                                  # [s, H, D], the bf16 outputs
+        acc = torch.zeros(s // 64, H, D)
+        for r in range(64):
+            acc = acc + x.view(s // 64, 64, H, D)[:, r]
+        assert torch.equal(sums[0, 0], acc.to(torch.bfloat16).permute(1, 0, 2))
+        if bf16_mean:
+            want = (acc.to(torch.bfloat16).float() / 64.0).to(torch.bfloat16).float()
+            assert torch.equal(mean[0, 0], want.permute(1, 0, 2))
+    assert torch.equal(v[0, 0], src.view(s, H, D))             # v passes through
