@@ -176,10 +176,20 @@ class Runner:
         self.lib = _capi.load()
         B, S, H, D = q.shape
         self.p = _capi.problem(B, S, H, D, t_seq_len, select_ratio=select_ratio, flat_ratio=flat_ratio)
+        # input and result dtypes as the drop-in sets them (bf16 for the 480p /
+        # 720p workloads; f32 for configuration 1)
+        import importlib
+        esa = importlib.import_module("in_context_sparse_attention.editing_sparse_attention")
+        dt = {torch.bfloat16: _capi.ICSA_BF16, torch.float32: _capi.ICSA_F32}
+        outc_dt, ca_dt, out_dt = esa._result_dtypes(q.dtype, k.dtype, v.dtype, 1.0)
+        self.p.q_dtype, self.p.k_dtype, self.p.v_dtype = dt[q.dtype], dt[k.dtype], dt[v.dtype]
+        self.p.out_dtype = dt[out_dt]
+        self.p.outc_bf16 = int(outc_dt == torch.bfloat16)
+        self.p.ca_bf16 = int(ca_dt == torch.bfloat16)
         self.L = _capi.workspace_layout(self.p)
         self.size = self.lib.icsa_workspace_size(ctypes.byref(self.p))
         self.ws = torch.empty(self.size, dtype=torch.uint8, device=q.device)
-        self.out = torch.empty_like(q)
+        self.out = torch.empty(q.shape, dtype=out_dt, device=q.device)
         self.q, self.k, self.v = q, k, v
         self.side = torch.cuda.Stream(device=q.device)
         self.fork, self.join = torch.cuda.Event(), torch.cuda.Event()
@@ -799,7 +809,8 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": ms, "unit": "ms/call", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
-                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded blurred-field generator)",
+                "vs_baseline": None, "dtype": "f32" if w.dtype == torch.float32 else "bf16",
+                "data": "synthetic (seeded blurred-field generator)",
                 "config": config_dict(w, world),
                 "stages_ms": stage,
                 "roofline": {"bound": "tensor", "kernel": "dense_pair_kernel (dense attention of the flat blocks, SM pairs)",
